@@ -1,0 +1,153 @@
+/*
+ * orthossm_b200 — C ABI of the B200-native Cheby-RKV hot path.
+ *
+ * Plain pointers and sizes; no torch types.  Every entry point is
+ * stream-ordered on the caller's stream, allocates nothing, and returns an
+ * ossm_status.  Device pointers are caller-allocated.  Tensors are row-major
+ * and contiguous along the channel axis; [B,S,D] activations take explicit
+ * batch / token strides in elements.
+ *
+ * Reference interfaces replaced (paths relative to the Eddym06/OrthoSSM root):
+ *   ossm_cheby_ema_fwd   <- _fused_clenshaw_ema_kernel launch
+ *                           (sdpc_kernel.py:988-1209, launched as in
+ *                           precision_tests.py:60-72) generalised to per-head
+ *                           and per-token decay, carried state and bf16 I/O;
+ *                           also the fast path _fast_path_forward
+ *                           (sdpc_kernel.py:1708-1744) via flags.
+ *   ossm_cheby_rkv_lion  <- the chunk loop of apply_cheby_rkv_v10
+ *                           (sdpc_kernel.py:2574-2606) around
+ *                           FusedChebyRKVv10.forward (:2352-2433) and
+ *                           _launch_ortho_megakernel / _ortho_megakernel
+ *                           (:2290-2344, :1889-2287): forward + local TTT
+ *                           gradient + inline Lion for every chunk, in one
+ *                           launch.
+ */
+#ifndef ORTHOSSM_B200_H
+#define ORTHOSSM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st* ossm_stream_t;
+
+enum ossm_status {
+  OSSM_OK = 0,
+  OSSM_EINVAL = 1,    /* bad shape, pointer, alignment or flag */
+  OSSM_ELAUNCH = 2,   /* CUDA launch / runtime error */
+  OSSM_ETIMEOUT = 3,  /* a bounded device-side wait gave up (see ossm_workspace_status) */
+  OSSM_ECOMM = 4,     /* multi-GPU exchange error */
+  OSSM_EWORKSPACE = 5 /* workspace missing or too small */
+};
+
+enum ossm_dtype { OSSM_F32 = 0, OSSM_BF16 = 1 };
+
+/* Chebyshev evaluation mode (low 2 bits of flags). */
+#define OSSM_EVAL_CLENSHAW 0u      /* exact degree-K Clenshaw (sdpc_kernel.py:1147-1156) */
+#define OSSM_EVAL_LUT 1u           /* 256-point half table + linear interpolation (:1098-1138) */
+#define OSSM_EVAL_CLENSHAW_DEG4 2u /* megakernel USE_LUT=False: only c_0..c_3 (:2073-2077) */
+#define OSSM_EVAL_MASK 3u
+/* Fast-path semantics (sdpc_kernel.py:1722-1739): x.sign() softsign with
+ * sign(0)=0 and NaN -> 0, and unclamped exact tanh. */
+#define OSSM_F_FASTPATH (1u << 2)
+/* Force correctly-rounded-grade tanh/softsign even for bf16 output. */
+#define OSSM_F_PRECISE (1u << 3)
+
+/* ---------------------------------------------------------------------------
+ * Fused softsign -> Chebyshev -> gamma_h damping -> tanh -> lambda-EMA scan.
+ *
+ *   xn = softsign(x); y_h = sum_k c[b,h,k,j] T_k(xn); z = gamma_h y,
+ *   gamma_h = 0.98 - 0.06 h / H; u = tanh(clamp(z, -4, 4)) (0 where x is NaN);
+ *   s_t = clamp(a_t s_{t-1} + (1 - a_t) u_t, -1, 1), s_{-1} = init_state.
+ *   a_t = momentum (lam_h == NULL), lam_h[h], or with the gate
+ *   clamp(lam_h[h] + gate_scale * (sigmoid(gate_w[h] . x_t + gate_b[h]) - 0.5),
+ *         gate_lo, gate_hi).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  int32_t B, S, H, head_dim, degree; /* head_dim power of two in [8,256]; 1 <= degree <= 8 */
+  const void* x;                     /* [B,S,H*head_dim], dtype x_dtype */
+  int32_t x_dtype;
+  int64_t x_stride_b, x_stride_s;    /* in elements; channel stride 1 */
+  const float* coeffs;               /* [B,H,degree,head_dim] contiguous */
+  const float* lam_h;                /* [H] or NULL */
+  float momentum;                    /* decay used when lam_h == NULL */
+  const float* gate_w;               /* [H, H*head_dim] or NULL (no dynamic decay) */
+  const float* gate_b;               /* [H] (required with gate_w) */
+  float gate_scale, gate_lo, gate_hi;
+  const float* lut;                  /* [8,256] table for OSSM_EVAL_LUT, else NULL */
+  const float* init_state;           /* [B,H*head_dim] or NULL (zeros) */
+  float* final_state;                /* [B,H*head_dim] or NULL */
+  void* out;                         /* [B,S,H*head_dim], dtype out_dtype */
+  int32_t out_dtype;
+  int64_t out_stride_b, out_stride_s;
+  float* tanh_out;                   /* optional f32 cache of u, same strides as out */
+  const float* lam_tok;              /* optional caller-computed per-token decay [B,S,H]
+                                        (e.g. from ossm_gate_decay); overrides the gate */
+  uint32_t flags;
+} ossm_fwd_args;
+
+/* Bytes of device workspace ossm_cheby_ema_fwd needs for these arguments.
+ * The workspace must be zero-filled once when first allocated and may then be
+ * reused by any number of calls that are ordered on one stream. */
+size_t ossm_fwd_workspace_bytes(const ossm_fwd_args* a);
+int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_t workspace_bytes,
+                       ossm_stream_t stream);
+
+/* The per-token decay of the gate alone: lam_tok[b,t,h] (f32, [B,S,H]) from
+ * a->x, a->gate_w, a->gate_b, a->lam_h, a->gate_scale/lo/hi.  Feeding the
+ * result back through a->lam_tok gives the same output as the gated call.
+ * No counterpart kernel in the reference (its gate is per batch,
+ * GatedComplexityPredictor, sdpc_kernel.py:1818-1830)
+ * configs[1] defines the per-token form. */
+int ossm_gate_decay(const ossm_fwd_args* a, float* lam_tok, ossm_stream_t stream);
+
+/* Read (and optionally clear) the sticky device status word of a workspace:
+ * OSSM_OK, or OSSM_ETIMEOUT if a look-back wait gave up.  Synchronises the
+ * stream. */
+int ossm_workspace_status(void* workspace, int clear, ossm_stream_t stream, int32_t* status);
+
+/* ---------------------------------------------------------------------------
+ * Reference-mode TTT: apply_cheby_rkv_v10's full path over the whole sequence.
+ * For each chunk of `chunk` tokens: EMA from zero with scalar momentum, output
+ * (rounded to bf16 as the reference does), local gated-error gradient
+ * g_k = sum_t e_t sigmoid(3|e_t|) T_k(xn_t) / (L-1), e_t = xn_{t+1} - s_t,
+ * then Lion: c <- (lam_eff - lr wd) c + lr (k+1)^-1.5 sign(b1 m + (1-b1) g),
+ * m <- b2 m + (1-b2) g, with lam_h / lr_scale_h of _get_lion_constants
+ * (sdpc_kernel.py:1423-1437).  coeffs and momentum are updated in place.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  int32_t B, S, H, head_dim, degree, chunk;
+  const void* x;                  /* [B,S,D]; rounded to bf16 on load when f32 */
+  int32_t x_dtype;
+  int64_t x_stride_b, x_stride_s;
+  float* coeffs;                  /* [B,H,degree,head_dim], in/out */
+  float* momentum;                /* [B,H,degree,head_dim], in/out */
+  const float* gate_global;       /* [B] lr multiplier or NULL */
+  const float* dynamic_lambda;    /* [B] forget-factor modulation or NULL */
+  float ema_momentum, base_lr, beta1, beta2, weight_decay;
+  const float* lut;               /* [8,256] for OSSM_EVAL_LUT */
+  void* out;                      /* [B,S,D] */
+  int32_t out_dtype;
+  int64_t out_stride_b, out_stride_s;
+  float* tanh_out;                /* optional f32 [B,S,D] (contiguous strides of out) */
+  float* final_state;             /* optional [B,D]: EMA state at the end of the last chunk */
+  uint32_t flags;                 /* OSSM_EVAL_* */
+} ossm_lion_args;
+
+int ossm_cheby_rkv_lion(const ossm_lion_args* a, ossm_stream_t stream);
+
+/* Library metadata. */
+const char* ossm_version(void);
+const char* ossm_status_string(int status);
+/* sizeof() of the argument structs, so bindings can check their layout. */
+size_t ossm_sizeof_fwd_args(void);
+size_t ossm_sizeof_lion_args(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ORTHOSSM_B200_H */

@@ -1,0 +1,13 @@
+"""orthossm_b200 — B200-native (sm_100a) OrthoSSM Cheby-RKV hot path.
+
+Public API mirrors the reference's ``sdpc_kernel`` op surface; see
+``orthossm_b200.sdpc_kernel``.  Kernels live in ``csrc/`` behind the C ABI of
+``include/orthossm_b200.h``; ``python -m orthossm_b200.build`` builds it.
+"""
+from .sdpc_kernel import (  # noqa: F401
+    BASELINE_LAMBDA, LUT_TABLE_SIZE, MAX_DEGREE, MULTI_SCALE_LAMBDA, FusedChebyRKVv10,
+    GatedComplexityPredictor, apply_cheby_rkv_core, apply_cheby_rkv_v10, cheby_ema_forward,
+    gate_decay, get_chebyshev_lut, init_chebyshev_coefficients, workspace_status,
+)
+
+__version__ = "0.1.0"

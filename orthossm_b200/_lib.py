@@ -1,0 +1,101 @@
+"""ctypes binding of the orthossm_b200 C ABI (include/orthossm_b200.h).
+
+The shared library is built in-tree by ``orthossm_b200.build``.  There is no
+fallback: if the library cannot be loaded, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+from . import build as _build
+
+OSSM_OK, OSSM_EINVAL, OSSM_ELAUNCH, OSSM_ETIMEOUT, OSSM_ECOMM, OSSM_EWORKSPACE = range(6)
+OSSM_F32, OSSM_BF16 = 0, 1
+OSSM_EVAL_CLENSHAW, OSSM_EVAL_LUT, OSSM_EVAL_CLENSHAW_DEG4 = 0, 1, 2
+OSSM_F_FASTPATH = 1 << 2
+OSSM_F_PRECISE = 1 << 3
+
+EXPORTED = (
+    "ossm_fwd_workspace_bytes", "ossm_cheby_ema_fwd", "ossm_gate_decay", "ossm_workspace_status",
+    "ossm_cheby_rkv_lion", "ossm_version", "ossm_status_string",
+    "ossm_sizeof_fwd_args", "ossm_sizeof_lion_args",
+)
+
+_vp = C.c_void_p
+_i32 = C.c_int32
+_i64 = C.c_int64
+_f32 = C.c_float
+
+
+class FwdArgs(C.Structure):
+    _fields_ = [
+        ("B", _i32), ("S", _i32), ("H", _i32), ("head_dim", _i32), ("degree", _i32),
+        ("x", _vp), ("x_dtype", _i32), ("x_stride_b", _i64), ("x_stride_s", _i64),
+        ("coeffs", _vp), ("lam_h", _vp), ("momentum", _f32),
+        ("gate_w", _vp), ("gate_b", _vp), ("gate_scale", _f32), ("gate_lo", _f32), ("gate_hi", _f32),
+        ("lut", _vp), ("init_state", _vp), ("final_state", _vp),
+        ("out", _vp), ("out_dtype", _i32), ("out_stride_b", _i64), ("out_stride_s", _i64),
+        ("tanh_out", _vp), ("lam_tok", _vp), ("flags", C.c_uint32),
+    ]
+
+
+class LionArgs(C.Structure):
+    _fields_ = [
+        ("B", _i32), ("S", _i32), ("H", _i32), ("head_dim", _i32), ("degree", _i32), ("chunk", _i32),
+        ("x", _vp), ("x_dtype", _i32), ("x_stride_b", _i64), ("x_stride_s", _i64),
+        ("coeffs", _vp), ("momentum", _vp), ("gate_global", _vp), ("dynamic_lambda", _vp),
+        ("ema_momentum", _f32), ("base_lr", _f32), ("beta1", _f32), ("beta2", _f32),
+        ("weight_decay", _f32),
+        ("lut", _vp), ("out", _vp), ("out_dtype", _i32), ("out_stride_b", _i64), ("out_stride_s", _i64),
+        ("tanh_out", _vp), ("final_state", _vp), ("flags", C.c_uint32),
+    ]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _declare(lib):
+    lib.ossm_fwd_workspace_bytes.restype = C.c_size_t
+    lib.ossm_fwd_workspace_bytes.argtypes = [C.POINTER(FwdArgs)]
+    lib.ossm_cheby_ema_fwd.restype = C.c_int
+    lib.ossm_cheby_ema_fwd.argtypes = [C.POINTER(FwdArgs), _vp, C.c_size_t, _vp]
+    lib.ossm_gate_decay.restype = C.c_int
+    lib.ossm_gate_decay.argtypes = [C.POINTER(FwdArgs), _vp, _vp]
+    lib.ossm_workspace_status.restype = C.c_int
+    lib.ossm_workspace_status.argtypes = [_vp, C.c_int, _vp, C.POINTER(_i32)]
+    lib.ossm_cheby_rkv_lion.restype = C.c_int
+    lib.ossm_cheby_rkv_lion.argtypes = [C.POINTER(LionArgs), _vp]
+    lib.ossm_version.restype = C.c_char_p
+    lib.ossm_status_string.restype = C.c_char_p
+    lib.ossm_status_string.argtypes = [C.c_int]
+    lib.ossm_sizeof_fwd_args.restype = C.c_size_t
+    lib.ossm_sizeof_lion_args.restype = C.c_size_t
+    if lib.ossm_sizeof_fwd_args() != C.sizeof(FwdArgs) or lib.ossm_sizeof_lion_args() != C.sizeof(LionArgs):
+        raise RuntimeError("orthossm_b200: ctypes struct layout does not match the C ABI")
+    return lib
+
+
+def lib():
+    """Load (building first if the library is absent and nvcc exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = _build.lib_path()
+            if not os.path.exists(path):
+                try:
+                    path = _build.build()
+                except Exception as e:  # no silent fallback: the op cannot run
+                    raise RuntimeError(f"orthossm_b200: CUDA library missing and build failed: {e}")
+            _lib = _declare(C.CDLL(path))
+    return _lib
+
+
+def check(status: int, what: str):
+    if status != OSSM_OK:
+        msg = lib().ossm_status_string(status).decode()
+        raise RuntimeError(f"orthossm_b200: {what} failed: {msg} (status {status})")

@@ -1,0 +1,359 @@
+"""Host-side mirror of the reference op API (Eddym06/OrthoSSM ``sdpc_kernel.py``).
+
+Same names, argument meanings and return values as the reference's public
+surface for the Cheby-RKV path, backed by hand-written sm_100a CUDA through
+the C ABI in ``include/orthossm_b200.h``:
+
+* ``apply_cheby_rkv_v10`` / ``apply_cheby_rkv_core`` (sdpc_kernel.py:2522-2610)
+* ``FusedChebyRKVv10.apply`` (:2351-2515, 16 positional arguments)
+* ``get_chebyshev_lut`` / ``LUT_TABLE_SIZE`` / ``MAX_DEGREE`` (:59-96)
+* ``MULTI_SCALE_LAMBDA`` (:1416), ``init_chebyshev_coefficients`` (:1833-1867),
+  ``GatedComplexityPredictor`` (:1818-1830)
+
+plus the BASELINE-semantics forward ``cheby_ema_forward`` (per-head decay,
+per-token dynamic decay from a Linear(D->H) gate, carried state, bf16 I/O).
+
+Tensors must live on a CUDA device; there is no CPU path and no fallback.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+import torch.nn as nn
+
+from . import _lib as L
+
+LUT_TABLE_SIZE: int = 256
+MAX_DEGREE: int = 8
+MULTI_SCALE_LAMBDA = [0.9995, 0.9995, 0.997, 0.997, 0.995, 0.995, 0.97, 0.95]
+BASELINE_LAMBDA = [0.9995, 0.9995, 0.997, 0.997, 0.995, 0.995, 0.95, 0.95]
+
+_DT = {torch.float32: L.OSSM_F32, torch.bfloat16: L.OSSM_BF16}
+
+
+# ----------------------------------------------------------------------------
+# reference helpers
+# ----------------------------------------------------------------------------
+
+def _build_chebyshev_lut(table_size: int = LUT_TABLE_SIZE, max_degree: int = MAX_DEGREE):
+    """T_k(u) for u on a uniform grid of [0, 1] (half table; odd degrees are
+    mirrored with the sign of x), float32 [max_degree, table_size]."""
+    u = torch.linspace(0.0, 1.0, table_size)
+    T = torch.empty(max_degree, table_size)
+    T[0] = 1.0
+    if max_degree > 1:
+        T[1] = u
+    for k in range(2, max_degree):
+        T[k] = 2.0 * u * T[k - 1] - T[k - 2]
+    return T
+
+
+_LUT_CPU = _build_chebyshev_lut()
+_LUT_DEV: dict = {}
+_LUT_LOCK = threading.Lock()
+
+
+def get_chebyshev_lut(device):
+    """Per-device cached LUT (thread safe)."""
+    key = torch.device(device)
+    t = _LUT_DEV.get(key)
+    if t is None:
+        with _LUT_LOCK:
+            t = _LUT_DEV.get(key)
+            if t is None:
+                t = _LUT_CPU.to(key).contiguous()
+                _LUT_DEV[key] = t
+    return t
+
+
+class GatedComplexityPredictor(nn.Module):
+    """Global TTT gate from mean(x): Linear(D, D/4) - SiLU - Linear(D/4, 1) - Sigmoid."""
+
+    def __init__(self, d_model):
+        super().__init__()
+        self.net = nn.Sequential(nn.Linear(d_model, d_model // 4), nn.SiLU(),
+                                 nn.Linear(d_model // 4, 1), nn.Sigmoid())
+
+    def forward(self, x_mean):
+        return self.net(x_mean)
+
+
+def init_chebyshev_coefficients(batch, n_heads, degree, head_dim, device):
+    """Spectral init c ~ N(0, (0.1/(k+1))^2) with heads orthogonalised by QR
+    (or a Parseval tight frame by SVD when degree*head_dim < n_heads)."""
+    k = torch.arange(degree, device=device, dtype=torch.float32)
+    sigma = (0.1 / (k + 1.0)).view(1, 1, degree, 1)
+    c = torch.randn(batch, n_heads, degree, head_dim, device=device) * sigma
+    if n_heads < 2:
+        return c
+    flat = c.reshape(batch, n_heads, degree * head_dim)
+    norms = flat.norm(dim=2, keepdim=True)
+    if degree * head_dim >= n_heads:
+        q, _ = torch.linalg.qr(flat.transpose(1, 2))
+        return (q.transpose(1, 2) * norms).reshape(batch, n_heads, degree, head_dim)
+    unit = flat / (norms + 1e-8)
+    rank = min(n_heads, degree * head_dim)
+    scale = (n_heads / rank) ** 0.5
+    for b in range(batch):
+        U, _, Vh = torch.linalg.svd(unit[b], full_matrices=False)
+        unit[b] = U[:, :rank] @ Vh[:rank] * scale
+    return (unit * norms).reshape(batch, n_heads, degree, head_dim)
+
+
+# ----------------------------------------------------------------------------
+# workspace (look-back flags / aggregates); one per (device, stream)
+# ----------------------------------------------------------------------------
+
+_WS: dict = {}
+_WS_LOCK = threading.Lock()
+
+
+def _workspace(device, stream, nbytes):
+    key = (device, stream.cuda_stream)
+    with _WS_LOCK:
+        ws = _WS.get(key)
+        if ws is None or ws.numel() < nbytes:
+            # zero-filled once: ticket / epoch / flags start at 0
+            ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+            _WS[key] = ws
+    return ws
+
+
+def workspace_status(device=None, clear=True):
+    """Sticky device status of the current stream's workspace (0 = ok,
+    3 = a look-back wait timed out).  Synchronises the stream."""
+    device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(device)
+    ws = _WS.get((device, stream.cuda_stream))
+    if ws is None:
+        return 0
+    st = L._i32(0)
+    L.check(L.lib().ossm_workspace_status(ws.data_ptr(), int(clear), stream.cuda_stream, L.C.byref(st)),
+            "workspace_status")
+    return int(st.value)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("orthossm_b200 ops run on CUDA tensors only (no CPU path)")
+
+
+def _rowmajor(x):
+    """[B,S,D] with unit channel stride (copy otherwise)."""
+    return x if x.stride(-1) == 1 else x.contiguous()
+
+
+# ----------------------------------------------------------------------------
+# BASELINE-semantics forward
+# ----------------------------------------------------------------------------
+
+def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,
+                      gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None,
+                      out_dtype=None, return_tanh=False, eval_mode="clenshaw",
+                      fast_path_semantics=False, precise=None, out=None, final_state=None,
+                      lam_tok=None):
+    """Fused softsign -> degree-K Chebyshev -> gamma_h -> tanh -> lambda-EMA.
+
+    x: [B,S,D] float32 or bfloat16 (CUDA); coeffs: [B,H,K,hd] float32.
+    lambda_per_head: [H] decay per head (None: scalar ``ema_momentum``).
+    gate_weight [H,D] / gate_bias [H]: per-token decay
+    ``clamp(lambda_h + gate_scale*(sigmoid(W x_t + b) - 0.5), *gate_range)``.
+    init_state: [B,D] float32 carried-in EMA state (None: zeros).
+    lam_tok: optional precomputed per-token decay [B,S,H] float32 (e.g. from
+    ``gate_decay``); overrides the gate.
+    Returns (out [B,S,D] in out_dtype (default x.dtype), final_state [B,D] f32)
+    and the f32 tanh cache when ``return_tanh``."""
+    _need_cuda(x, coeffs)
+    x = _rowmajor(x)
+    if x.dtype not in _DT:
+        x = x.float()
+    B, S, D = x.shape
+    coeffs = coeffs.contiguous().float()
+    H, K, hd = coeffs.shape[1], coeffs.shape[2], coeffs.shape[3]
+    if H * hd != D or coeffs.shape[0] != B:
+        raise ValueError(f"coeffs {tuple(coeffs.shape)} do not match x {tuple(x.shape)}")
+    dev = x.device
+    odt = out_dtype or x.dtype
+    if out is None:
+        out = torch.empty(B, S, D, device=dev, dtype=odt)
+    if final_state is None:
+        final_state = torch.empty(B, D, device=dev, dtype=torch.float32)
+    lam = None
+    if lambda_per_head is not None:
+        lam = torch.as_tensor(lambda_per_head, dtype=torch.float32, device=dev).contiguous()
+    if gate_weight is not None:
+        gate_weight = gate_weight.to(dev, torch.float32).contiguous()
+        gate_bias = gate_bias.to(dev, torch.float32).contiguous()
+        if lam is None:
+            lam = torch.full((H,), float(ema_momentum), device=dev)
+    if init_state is not None:
+        init_state = init_state.to(dev, torch.float32).contiguous()
+    if lam_tok is not None:
+        _need_cuda(lam_tok)
+        lam_tok = lam_tok.float().contiguous()
+        if tuple(lam_tok.shape) != (B, S, H):
+            raise ValueError(f"lam_tok must be [B,S,H] = {(B, S, H)}")
+    tanh = torch.empty(B, S, D, device=dev, dtype=torch.float32) if return_tanh else None
+    if tanh is not None and out.stride() != tanh.stride():
+        raise ValueError("tanh cache needs the output's strides")
+    flags = {"clenshaw": L.OSSM_EVAL_CLENSHAW, "lut": L.OSSM_EVAL_LUT,
+             "clenshaw_deg4": L.OSSM_EVAL_CLENSHAW_DEG4}[eval_mode]
+    if fast_path_semantics:
+        flags |= L.OSSM_F_FASTPATH
+    if precise:
+        flags |= L.OSSM_F_PRECISE
+    lut = get_chebyshev_lut(dev) if eval_mode == "lut" else None
+    a = L.FwdArgs(B=B, S=S, H=H, head_dim=hd, degree=K,
+                  x=x.data_ptr(), x_dtype=_DT[x.dtype], x_stride_b=x.stride(0), x_stride_s=x.stride(1),
+                  coeffs=coeffs.data_ptr(), lam_h=_ptr(lam), momentum=float(ema_momentum),
+                  gate_w=_ptr(gate_weight), gate_b=_ptr(gate_bias), gate_scale=float(gate_scale),
+                  gate_lo=float(gate_range[0]), gate_hi=float(gate_range[1]),
+                  lut=_ptr(lut), init_state=_ptr(init_state), final_state=_ptr(final_state),
+                  out=out.data_ptr(), out_dtype=_DT[out.dtype], out_stride_b=out.stride(0),
+                  out_stride_s=out.stride(1), tanh_out=_ptr(tanh), lam_tok=_ptr(lam_tok), flags=flags)
+    lib = L.lib()
+    nbytes = lib.ossm_fwd_workspace_bytes(L.C.byref(a))
+    if nbytes == 0:
+        L.check(L.OSSM_EINVAL, "cheby_ema_forward (argument check)")
+    stream = torch.cuda.current_stream(dev)
+    ws = _workspace(dev, stream, nbytes)
+    L.check(lib.ossm_cheby_ema_fwd(L.C.byref(a), ws.data_ptr(), ws.numel(), stream.cuda_stream),
+            "cheby_ema_forward")
+    if return_tanh:
+        return out, final_state, tanh
+    return out, final_state
+
+
+def gate_decay(x, gate_weight, gate_bias, lambda_per_head, *, gate_scale=0.008,
+               gate_range=(0.0, 1.0), out=None):
+    """Per-token decay of the dynamic-lambda gate, [B,S,H] float32:
+    ``clamp(lambda_h + gate_scale*(sigmoid(W x_t + b)[h] - 0.5), *gate_range)``."""
+    _need_cuda(x)
+    x = _rowmajor(x)
+    if x.dtype not in _DT:
+        x = x.float()
+    B, S, D = x.shape
+    dev = x.device
+    W = gate_weight.to(dev, torch.float32).contiguous()
+    bvec = gate_bias.to(dev, torch.float32).contiguous()
+    H = W.shape[0]
+    lam = torch.as_tensor(lambda_per_head, dtype=torch.float32, device=dev).contiguous()
+    if out is None:
+        out = torch.empty(B, S, H, device=dev, dtype=torch.float32)
+    a = L.FwdArgs(B=B, S=S, H=H, head_dim=D // H, degree=1, x=x.data_ptr(), x_dtype=_DT[x.dtype],
+                  x_stride_b=x.stride(0), x_stride_s=x.stride(1), coeffs=lam.data_ptr(),
+                  lam_h=lam.data_ptr(), gate_w=W.data_ptr(), gate_b=bvec.data_ptr(),
+                  gate_scale=float(gate_scale), gate_lo=float(gate_range[0]),
+                  gate_hi=float(gate_range[1]), out=x.data_ptr(), out_dtype=_DT[x.dtype],
+                  out_stride_b=x.stride(0), out_stride_s=x.stride(1))
+    stream = torch.cuda.current_stream(dev)
+    L.check(L.lib().ossm_gate_decay(L.C.byref(a), out.data_ptr(), stream.cuda_stream), "gate_decay")
+    return out
+
+
+# ----------------------------------------------------------------------------
+# reference op: apply_cheby_rkv_v10
+# ----------------------------------------------------------------------------
+
+def _per_batch(v, B, dev):
+    if v is None:
+        return None
+    t = torch.as_tensor(v, device=dev).float().reshape(-1)
+    if t.numel() < B:
+        t = t.expand(B) if t.numel() == 1 else t
+    return t[:B].contiguous()
+
+
+def _lion_full_path(x, coeffs, momentum_buf, n_heads, base_lr, ema_momentum, lion_beta1,
+                    lion_beta2, lion_wd, chunk_size, gate_global, dynamic_lambda, use_lut,
+                    out_dtype=torch.float32, final_state=None):
+    """All chunks of the reference's full path in one launch.  Returns
+    (out [B,S,D] bf16-rounded values, new coeffs, new momentum)."""
+    _need_cuda(x, coeffs)
+    x = _rowmajor(x)
+    if x.dtype not in _DT:
+        x = x.float()
+    B, S, D = x.shape
+    hd = D // n_heads
+    if hd * n_heads != D:
+        raise ValueError("D must be divisible by n_heads")
+    dev = x.device
+    c = coeffs.float().contiguous().clone()
+    m = momentum_buf.float().contiguous().clone() if momentum_buf is not None else torch.zeros_like(c)
+    K = c.shape[2]
+    if tuple(c.shape) != (B, n_heads, K, hd):
+        raise ValueError(f"coeffs {tuple(c.shape)} vs expected {(B, n_heads, K, hd)}")
+    out = torch.empty(B, S, D, device=dev, dtype=out_dtype)
+    lut = get_chebyshev_lut(dev) if use_lut else None
+    gg = _per_batch(gate_global, B, dev)
+    dl = _per_batch(dynamic_lambda, B, dev)
+    a = L.LionArgs(B=B, S=S, H=n_heads, head_dim=hd, degree=K, chunk=int(chunk_size),
+                   x=x.data_ptr(), x_dtype=_DT[x.dtype], x_stride_b=x.stride(0), x_stride_s=x.stride(1),
+                   coeffs=c.data_ptr(), momentum=m.data_ptr(), gate_global=_ptr(gg),
+                   dynamic_lambda=_ptr(dl), ema_momentum=float(ema_momentum), base_lr=float(base_lr),
+                   beta1=float(lion_beta1), beta2=float(lion_beta2), weight_decay=float(lion_wd),
+                   lut=_ptr(lut), out=out.data_ptr(), out_dtype=_DT[out_dtype],
+                   out_stride_b=out.stride(0), out_stride_s=out.stride(1), tanh_out=None,
+                   final_state=_ptr(final_state),
+                   flags=L.OSSM_EVAL_LUT if use_lut else L.OSSM_EVAL_CLENSHAW_DEG4)
+    stream = torch.cuda.current_stream(dev)
+    L.check(L.lib().ossm_cheby_rkv_lion(L.C.byref(a), stream.cuda_stream), "cheby_rkv_lion")
+    return out, c, m
+
+
+class FusedChebyRKVv10(torch.autograd.Function):
+    """One full-path call over the whole sequence as a single chunk
+    (reference: sdpc_kernel.py:2351-2515).  Same 16 positional arguments."""
+
+    @staticmethod
+    def forward(ctx, x, coeffs, momentum_buf, n_heads=4, base_lr=0.005, ema_momentum=0.9,
+                lion_beta1=0.9, lion_beta2=0.99, lion_wd=0.01, chunk_size=256, use_bf16=False,
+                gate_global=None, dynamic_lambda=None, use_lut=True, seq_threshold=384,
+                lion_max_norm=14.0):
+        S = x.shape[1]
+        out, c, m = _lion_full_path(x, coeffs, momentum_buf, n_heads, base_lr, ema_momentum,
+                                    lion_beta1, lion_beta2, lion_wd, S, gate_global,
+                                    dynamic_lambda, use_lut)
+        ctx.mark_non_differentiable(c, m)
+        return out, c, m
+
+    @staticmethod
+    def backward(ctx, grad_out, grad_c, grad_m):
+        raise NotImplementedError("orthossm_b200: backward of the Cheby-RKV op is not built yet")
+
+
+def apply_cheby_rkv_v10(x, coeffs, momentum_buf, n_heads=4, base_lr=0.005, ema_momentum=0.9,
+                        lion_beta1=0.9, lion_beta2=0.99, lion_wd=0.01, chunk_size=256,
+                        use_bf16=False, gate_global=None, dynamic_lambda=None, use_lut=True,
+                        seq_threshold=384, lion_max_norm=14.0):
+    """OrthoSSM V10 core op (reference: sdpc_kernel.py:2522-2606).
+
+    Returns (output float32 [B,S,D], new_coeffs, new_momentum).  Below
+    ``seq_threshold`` tokens: fast path (no TTT, coefficients returned
+    unchanged).  Otherwise the reference's chunked Lion TTT over
+    ``chunk_size``-token chunks, all chunks in one device launch.
+    ``use_bf16`` and ``lion_max_norm`` are accepted and, as in the reference's
+    live path, unused."""
+    B, S, D = x.shape
+    if coeffs.dtype != torch.float32:
+        coeffs = coeffs.float()
+    if momentum_buf is not None and momentum_buf.dtype != torch.float32:
+        momentum_buf = momentum_buf.float()
+    if seq_threshold > 0 and S < seq_threshold:
+        xf = x if x.dtype in _DT else x.float()
+        out, _ = cheby_ema_forward(xf, coeffs, ema_momentum=ema_momentum, fast_path_semantics=True,
+                                   out_dtype=torch.float32 if x.dtype != torch.bfloat16 else x.dtype)
+        return out, coeffs, momentum_buf
+    if torch.is_grad_enabled() and (x.requires_grad or coeffs.requires_grad):
+        raise NotImplementedError("orthossm_b200: backward of the Cheby-RKV op is not built yet")
+    return _lion_full_path(x, coeffs, momentum_buf, n_heads, base_lr, ema_momentum, lion_beta1,
+                           lion_beta2, lion_wd, chunk_size, gate_global, dynamic_lambda, use_lut)
+
+
+apply_cheby_rkv_core = apply_cheby_rkv_v10
