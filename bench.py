@@ -217,7 +217,7 @@ def run_ours(args):
     W = torch.from_numpy(W_np).to(dev)
     bvec = torch.from_numpy(b_np).to(dev)
     init = torch.from_numpy(init_np).to(dev)
-    lam = LAMBDA
+    lam = torch.tensor(LAMBDA, device=dev)  # device tensor: no host copy inside graph capture
     outs = [torch.empty(B, S, D, device=dev, dtype=torch.bfloat16) for _ in range(2)]
     fin = torch.empty(B, D, device=dev)
 

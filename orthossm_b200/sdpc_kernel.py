@@ -121,17 +121,18 @@ def _workspace(device, stream, nbytes):
 
 
 def workspace_status(device=None, clear=True):
-    """Sticky device status of the current stream's workspace (0 = ok,
-    3 = a look-back wait timed out).  Synchronises the stream."""
+    """Sticky device status over every workspace of a device (0 = ok,
+    3 = a look-back wait timed out).  Synchronises each workspace's stream."""
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    stream = torch.cuda.current_stream(device)
-    ws = _WS.get((device, stream.cuda_stream))
-    if ws is None:
-        return 0
-    st = L._i32(0)
-    L.check(L.lib().ossm_workspace_status(ws.data_ptr(), int(clear), stream.cuda_stream, L.C.byref(st)),
-            "workspace_status")
-    return int(st.value)
+    worst = 0
+    for (d, sptr), ws in list(_WS.items()):
+        if d != device:
+            continue
+        st = L._i32(0)
+        L.check(L.lib().ossm_workspace_status(ws.data_ptr(), int(clear), sptr, L.C.byref(st)),
+                "workspace_status")
+        worst = max(worst, int(st.value))
+    return worst
 
 
 def _ptr(t):
