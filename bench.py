@@ -41,6 +41,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--soak-s", type=float, default=1.5, help="loaded seconds sampled for clocks before timing")
+    ap.add_argument("--profile-once", action="store_true",
+                    help="3 warm-up steps + 1 step (gate, then scan with the decay), nothing else: for ncu")
     return ap.parse_args()
 
 
@@ -226,6 +228,16 @@ def run_ours(args):
                             init_state=init, out=outs[i % 2], final_state=fin)
 
     stream = torch.cuda.Stream(dev)
+    if args.profile_once:
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                step(i)
+            lt = O.gate_decay(xs[0], W, bvec, lam)
+            O.cheby_ema_forward(xs[0], c, lambda_per_head=lam, lam_tok=lt, init_state=init,
+                                out=outs[0], final_state=fin)
+        torch.cuda.synchronize()
+        print("profile-once done, status", O.workspace_status())
+        return
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 3)):
             step(i)
