@@ -56,6 +56,9 @@ enum ossm_dtype { OSSM_F32 = 0, OSSM_BF16 = 1 };
 #define OSSM_F_FASTPATH (1u << 2)
 /* Force correctly-rounded-grade tanh/softsign even for bf16 output. */
 #define OSSM_F_PRECISE (1u << 3)
+/* Use the generic forward kernel even where the TMA / tcgen05 path applies
+ * (the two paths compute the same function; used to test one against the other). */
+#define OSSM_F_GENERIC (1u << 4)
 
 /* ---------------------------------------------------------------------------
  * Fused softsign -> Chebyshev -> gamma_h damping -> tanh -> lambda-EMA scan.

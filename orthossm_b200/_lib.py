@@ -16,6 +16,7 @@ OSSM_F32, OSSM_BF16 = 0, 1
 OSSM_EVAL_CLENSHAW, OSSM_EVAL_LUT, OSSM_EVAL_CLENSHAW_DEG4 = 0, 1, 2
 OSSM_F_FASTPATH = 1 << 2
 OSSM_F_PRECISE = 1 << 3
+OSSM_F_GENERIC = 1 << 4
 
 EXPORTED = (
     "ossm_fwd_workspace_bytes", "ossm_cheby_ema_fwd", "ossm_gate_decay", "ossm_workspace_status",

@@ -37,6 +37,10 @@ OSSM_DEV void st4(__nv_bfloat16* p, float4 v) {
   u.y = pack_bf16x2(v.z, v.w);
   __stcs(reinterpret_cast<uint2*>(p), u);
 }
+OSSM_DEV void st2(float* p, float2 v) { __stcs(reinterpret_cast<float2*>(p), v); }
+OSSM_DEV void st2(__nv_bfloat16* p, float2 v) {
+  __stcs(reinterpret_cast<unsigned int*>(p), pack_bf16x2(v.x, v.y));
+}
 OSSM_DEV float bf16_round(float v) {  // round-to-nearest-even to bf16, as float
   return __bfloat162float(__float2bfloat16_rn(v));
 }

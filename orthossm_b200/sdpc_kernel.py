@@ -158,7 +158,7 @@ def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate
                       gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None,
                       out_dtype=None, return_tanh=False, eval_mode="clenshaw",
                       fast_path_semantics=False, precise=None, out=None, final_state=None,
-                      lam_tok=None):
+                      lam_tok=None, force_generic=False):
     """Fused softsign -> degree-K Chebyshev -> gamma_h -> tanh -> lambda-EMA.
 
     x: [B,S,D] float32 or bfloat16 (CUDA); coeffs: [B,H,K,hd] float32.
@@ -168,6 +168,8 @@ def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate
     init_state: [B,D] float32 carried-in EMA state (None: zeros).
     lam_tok: optional precomputed per-token decay [B,S,H] float32 (e.g. from
     ``gate_decay``); overrides the gate.
+    force_generic: run the generic kernel even where the TMA / tcgen05 path
+    applies (bf16 x, head_dim 64); both compute the same function.
     Returns (out [B,S,D] in out_dtype (default x.dtype), final_state [B,D] f32)
     and the f32 tanh cache when ``return_tanh``."""
     _need_cuda(x, coeffs)
@@ -209,6 +211,8 @@ def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate
         flags |= L.OSSM_F_FASTPATH
     if precise:
         flags |= L.OSSM_F_PRECISE
+    if force_generic:
+        flags |= L.OSSM_F_GENERIC
     lut = get_chebyshev_lut(dev) if eval_mode == "lut" else None
     a = L.FwdArgs(B=B, S=S, H=H, head_dim=hd, degree=K,
                   x=x.data_ptr(), x_dtype=_DT[x.dtype], x_stride_b=x.stride(0), x_stride_s=x.stride(1),
