@@ -330,11 +330,15 @@ __global__ void __launch_bounds__(kNT, 2) fwd_scan_kernel(const FwdParams p) {
     if (c > 0) {
       p.aggB[n * p.HD + tid] = chunkB;
       if (tid == 0) p.aggA[n] = chunkA;
-      __threadfence();
     }
   }
   __syncthreads();
-  if (c > 0 && tid == 0) st_release(p.lbflag + n, (epoch << 2) | 1u);
+  // barrier + a gpu-scope release fence in the publishing thread order the
+  // CTA's writes before the flag
+  if (c > 0 && tid == 0) {
+    __threadfence();
+    st_release(p.lbflag + n, (epoch << 2) | 1u);
+  }
 
   if (tid < p.HD) {
     float X = 0.f;  // state at the end of chunk c-1
@@ -365,10 +369,12 @@ __global__ void __launch_bounds__(kNT, 2) fwd_scan_kernel(const FwdParams p) {
     }
     carry_s[tid] = X;
     p.incB[n * p.HD + tid] = fmaf(chunkA, X, chunkB);
-    __threadfence();
   }
   __syncthreads();
-  if (tid == 0) st_release(p.lbflag + n, (epoch << 2) | 2u);
+  if (tid == 0) {
+    __threadfence();
+    st_release(p.lbflag + n, (epoch << 2) | 2u);
+  }
 
   // ---- phase 3: apply carries, write ---------------------------------------
   float rc[kV];

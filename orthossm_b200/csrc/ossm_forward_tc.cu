@@ -72,14 +72,6 @@ struct Params {
   uint32_t nunits;  // tickets per launch (clusters with the gate, CTAs without)
 };
 
-// Monomial coefficients of T_0..T_7 (T_k(x) = sum_m kChebMono[k][m] x^m).
-__constant__ float kChebMono[8][8] = {
-    {1, 0, 0, 0, 0, 0, 0, 0},         {0, 1, 0, 0, 0, 0, 0, 0},
-    {-1, 0, 2, 0, 0, 0, 0, 0},        {0, -3, 0, 4, 0, 0, 0, 0},
-    {1, 0, -8, 0, 8, 0, 0, 0},        {0, 5, 0, -20, 0, 16, 0, 0},
-    {-1, 0, 18, 0, -48, 0, 32, 0},    {0, -7, 0, 56, 0, -112, 0, 64},
-};
-
 OSSM_DEV float4 unpack_bf16x4(uint2 u) {
   return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
                      __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
@@ -116,12 +108,7 @@ __global__ void __launch_bounds__(kNT, 2) fwd_tc_kernel(const __grid_constant__ 
     fence_mbar_init();
     prefetch_tmap(&tmap);
   }
-  if (GATE) {
-    if (warp == 1) tmem_alloc(tmem_slot, 32);
-    tc_fence_before();
-    cluster_sync();  // every CTA of the cluster has started: DSMEM is addressable
-    tc_fence_after();
-  }
+  if (GATE && warp == 1) tmem_alloc(tmem_slot, 32);
   if (tid == 0 && crank == 0) {
     const uint32_t e = atomicAdd(&p.ws->epoch, 0u);
     __threadfence();
@@ -131,22 +118,19 @@ __global__ void __launch_bounds__(kNT, 2) fwd_tc_kernel(const __grid_constant__ 
       atomicExch(&p.ws->ticket, 0u);
       atomicExch(&p.ws->epoch, e + 1u);
     }
-    if (GATE) {
-      for (int r = 0; r < p.H; ++r) {
-        st_cluster_u32(map_smem(s_ticket, r), t);
-        st_cluster_u32(map_smem(s_epoch, r), e);
-      }
-    } else {
-      *s_ticket = t;
-      *s_epoch = e;
-    }
+    *s_ticket = t;
+    *s_epoch = e;
   }
-  if (GATE)
-    cluster_sync();  // ticket delivered to every CTA
-  else
+  uint32_t ticket, epoch;
+  if (GATE) {
+    cluster_sync();  // every CTA has started (DSMEM addressable) and rank 0 holds the ticket
+    ticket = ld_cluster_u32(map_smem(s_ticket, 0));
+    epoch = ld_cluster_u32(map_smem(s_epoch, 0));
+  } else {
     __syncthreads();
-  const uint32_t ticket = *s_ticket;
-  const uint32_t epoch = *s_epoch;
+    ticket = *s_ticket;
+    epoch = *s_epoch;
+  }
   int b, h, c;
   if (GATE) {
     c = (int)(ticket / p.B);
@@ -209,24 +193,36 @@ __global__ void __launch_bounds__(kNT, 2) fwd_tc_kernel(const __grid_constant__ 
 #pragma unroll
       for (int k = 0; k < 8; ++k) cf[k] = ck[k];
     } else {
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        double a0 = 0.0, a1 = 0.0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          a0 += (double)kChebMono[k][m] * (double)ck[k].x;
-          a1 += (double)kChebMono[k][m] * (double)ck[k].y;
-        }
-        cf[m] = make_float2((float)(a0 * (double)gamma), (float)(a1 * (double)gamma));
-      }
+      // T_0..T_7 in the monomial basis: sum_k c_k T_k(x) = sum_m a_m x^m
+      const float2 g2 = make_float2(gamma, gamma);
+      auto lin = [&](float w0, int k0, float w1, int k1, float w2, int k2, float w3, int k3) {
+        float2 r = make_float2(0.f, 0.f);
+        if (k0 >= 0) r = fma2(make_float2(w0, w0), ck[k0], r);
+        if (k1 >= 0) r = fma2(make_float2(w1, w1), ck[k1], r);
+        if (k2 >= 0) r = fma2(make_float2(w2, w2), ck[k2], r);
+        if (k3 >= 0) r = fma2(make_float2(w3, w3), ck[k3], r);
+        return mul2(r, g2);
+      };
+      cf[0] = lin(1.f, 0, -1.f, 2, 1.f, 4, -1.f, 6);
+      cf[1] = lin(1.f, 1, -3.f, 3, 5.f, 5, -7.f, 7);
+      cf[2] = lin(2.f, 2, -8.f, 4, 18.f, 6, 0.f, -1);
+      cf[3] = lin(4.f, 3, -20.f, 5, 56.f, 7, 0.f, -1);
+      cf[4] = lin(8.f, 4, -48.f, 6, 0.f, -1, 0.f, -1);
+      cf[5] = lin(16.f, 5, -112.f, 7, 0.f, -1, 0.f, -1);
+      cf[6] = lin(32.f, 6, 0.f, -1, 0.f, -1, 0.f, -1);
+      cf[7] = lin(64.f, 7, 0.f, -1, 0.f, -1, 0.f, -1);
     }
   }
-  if (GATE) __syncthreads();  // wsm complete before the MMA issue
+  if (GATE) {
+    tc_fence_before();
+    __syncthreads();  // wsm complete and the TMEM address visible before the MMA issue
+  }
 
   // ---- wait for the tile ------------------------------------------------------
   bool ok_tma = mbar_wait(tma_bar, 0);
 
   // ---- 2. gate MMA issue (one thread) -----------------------------------------
+  if (GATE) tc_fence_after();
   const uint32_t tmem = GATE ? *tmem_slot : 0u;
   if (GATE && tid == 0) {
     tc_fence_after();
@@ -358,11 +354,15 @@ __global__ void __launch_bounds__(kNT, 2) fwd_tc_kernel(const __grid_constant__ 
     if (c > 0) {
       p.aggB[n * kHD + tid] = chunkB;
       if (tid == 0) p.aggA[n] = chunkA;
-      __threadfence();
     }
   }
   __syncthreads();
-  if (c > 0 && tid == 0) st_release(p.lbflag + n, (epoch << 2) | 1u);
+  // the CTA's writes are ordered before the flag by the barrier plus a
+  // gpu-scope release fence in the publishing thread
+  if (c > 0 && tid == 0) {
+    __threadfence();
+    st_release(p.lbflag + n, (epoch << 2) | 1u);
+  }
   if (c > 0 && warp == 0) {
     // warp-wide window: lane i probes chunk (base - i); nearest inclusive wins
     int base = c - 1, kincl = -1;
@@ -388,7 +388,20 @@ __global__ void __launch_bounds__(kNT, 2) fwd_tc_kernel(const __grid_constant__ 
       const int k = *s_kincl;
       if (k >= 0) {
         X = __ldcg(p.incB + (n - (size_t)(c - k)) * kHD + tid);
-        for (int j = k + 1; j < c; ++j) {
+        // fold forward 4 chunks at a time; the loads do not depend on X
+        int j = k + 1;
+        for (; j + 4 <= c; j += 4) {
+          float aa[4], bb[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const size_t nj = n - (size_t)(c - (j + u));
+            aa[u] = __ldcg(p.aggA + nj);
+            bb[u] = __ldcg(p.aggB + nj * kHD + tid);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) X = fmaf(aa[u], X, bb[u]);
+        }
+        for (; j < c; ++j) {
           const size_t nj = n - (size_t)(c - j);
           X = fmaf(__ldcg(p.aggA + nj), X, __ldcg(p.aggB + nj * kHD + tid));
         }
@@ -399,10 +412,12 @@ __global__ void __launch_bounds__(kNT, 2) fwd_tc_kernel(const __grid_constant__ 
     }
     carry_s[tid] = X;
     p.incB[n * kHD + tid] = fmaf(chunkA, X, chunkB);
-    __threadfence();
   }
   __syncthreads();
-  if (tid == 0) st_release(p.lbflag + n, (epoch << 2) | 2u);
+  if (tid == 0) {
+    __threadfence();
+    st_release(p.lbflag + n, (epoch << 2) | 2u);
+  }
 
   // ---- 5. outputs -----------------------------------------------------------------
   {
