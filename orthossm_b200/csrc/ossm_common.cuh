@@ -129,7 +129,8 @@ struct WsHeader {
   uint32_t epoch;   // launch counter tagging look-back flags; advanced by the last CTA
   uint32_t status;  // sticky error word (OSSM_ETIMEOUT), cleared by the host
   uint32_t timeouts;
-  uint32_t pad[60];
+  uint32_t exited;  // persistent units that have left (the last one resets ticket/epoch)
+  uint32_t pad[59];
 };
 static_assert(sizeof(WsHeader) == 256, "header is one 256-byte block");
 
