@@ -50,7 +50,8 @@ constexpr int kOffExclA = kOffAggA + 64;               // [8] f32
 constexpr int kOffCarry = kOffExclA + 64;              // [64] f32
 constexpr int kOffLam = kOffCarry + kHD * 4;           // [256] float4 (lam, lam, 1-lam, 1-lam)
 constexpr int kOffPart = kOffLam + kL * 16;            // [2 items][8 src][256] f32 partial logits
-constexpr int kOffBar = kOffPart + 2 * kMaxH * kL * 4; // mbarriers + scalars
+constexpr int kOffCoef = kOffPart + 2 * kMaxH * kL * 4; // [2 items][8][64] f32 coefficients of (b, h)
+constexpr int kOffBar = kOffCoef + 2 * 8 * kHD * 4;    // mbarriers + scalars
 constexpr int kSmemBytes = kOffBar + 128;
 constexpr int kSmemAlloc = kSmemBytes + 1024;          // slack for 1024-byte alignment
 
@@ -185,11 +186,14 @@ __global__ void __launch_bounds__(kNT, 2)
       h = rem % p.H;
     }
   };
-  auto issue_load = [&](uint32_t t, int buf) {  // one thread
+  auto issue_load = [&](uint32_t t, int buf) {  // one thread: x tile + the (b, h) coefficients
     int b, h, c;
     decode(t, b, h, c);
-    mbar_expect_tx(tma_bar + buf, kTile);
+    const uint32_t cbytes = (uint32_t)p.K * kHD * 4;
+    mbar_expect_tx(tma_bar + buf, kTile + cbytes);
     tma_load_3d(sm + kOffX + buf * kTile, &tmap_x, tma_bar + buf, h * kHD, c * kL, b);
+    bulk_load(sm + kOffCoef + buf * (8 * kHD * 4), p.coeffs + ((size_t)(b * p.H + h) * p.K) * kHD, cbytes,
+              tma_bar + buf);
   };
   if (tid == 0) {
     if (tk_s[0] < p.nunits) issue_load(tk_s[0], 0);
@@ -212,16 +216,27 @@ __global__ void __launch_bounds__(kNT, 2)
     const int ch0 = h * kHD + j0;
     const float gamma = 0.98f - 0.06f * (float)h / (float)p.H;
 
-    // coefficients of (b, h): raw Chebyshev (precise) or gamma-folded monomial
+    // the ticket two items ahead: issued now, consumed after the evaluation
+    uint32_t t_ahead = 0;
+    if (tid == 0 && leader) t_ahead = atomicAdd(&p.ws->ticket, 1u);
+    // per-token decay supplied by the caller: load early as well
+    const int tg = t0 + tid;
+    float lam_in = 1.f;
+    if (!GATE) {
+      lam_in = p.lam_tok ? (tg < p.S ? __ldg(p.lam_tok + ((size_t)b * p.S + tg) * p.H + h) : 1.f)
+                         : (p.lam_h ? __ldg(p.lam_h + h) : p.momentum);
+    }
+
+    ok &= mbar_wait(tma_bar + buf, (uint32_t)(i >> 1) & 1u);
+
+    // coefficients of (b, h) from the tile's transaction: raw Chebyshev
+    // (precise) or gamma-folded monomial
     float2 cf[8];
     {
-      const float* cb = p.coeffs + ((size_t)(b * p.H + h) * p.K) * kHD + j0;
+      const float* cs = reinterpret_cast<const float*>(sm + kOffCoef + buf * (8 * kHD * 4)) + j0;
       float2 ck[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        ck[k] = make_float2(0.f, 0.f);
-        if (k < p.K) ck[k] = __ldg(reinterpret_cast<const float2*>(cb + (size_t)k * kHD));
-      }
+      for (int k = 0; k < 8; ++k) ck[k] = k < p.K ? *reinterpret_cast<const float2*>(cs + k * kHD) : make_float2(0.f, 0.f);
       if (PRECISE) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) cf[k] = ck[k];
@@ -229,8 +244,6 @@ __global__ void __launch_bounds__(kNT, 2)
         cheb_to_mono(ck, gamma, cf);
       }
     }
-
-    ok &= mbar_wait(tma_bar + buf, (uint32_t)(i >> 1) & 1u);
 
     // gate MMA (one thread): D[tokens][16] in TMEM
     if (GATE && tid == 0) {
@@ -284,8 +297,7 @@ __global__ void __launch_bounds__(kNT, 2)
       sl[r] = make_float2(x0 == x0 ? u0 : 0.f, x1 == x1 ? u1v : 0.f);  // NaN input -> 0 (sdpc_kernel.py:1164)
     }
 
-    // decay of each token; the ticket two items ahead is taken here
-    const int tg = t0 + tid;
+    // decay of each token; publish the ticket taken above
     if (GATE) {
       ok &= mbar_wait(mma_bar, (uint32_t)i & 1u);
       tc_fence_after();
@@ -295,10 +307,8 @@ __global__ void __launch_bounds__(kNT, 2)
       const int tok = mt * 128 + q4 * 32 + lane;
       float* part_i = part_s + buf * (kMaxH * kL);
       for (int n = 0; n < p.H; ++n) st_cluster_f32(map_smem(part_i + crank * kL + tok, n), v[n] + v[n + 8]);
-      if (tid == 0 && leader) {
-        const uint32_t t2 = atomicAdd(&p.ws->ticket, 1u);
-        for (int r = 0; r < p.H; ++r) st_cluster_u32(map_smem(tk_s + (i + 2) % 3, r), t2);
-      }
+      if (tid == 0 && leader)
+        for (int r = 0; r < p.H; ++r) st_cluster_u32(map_smem(tk_s + (i + 2) % 3, r), t_ahead);
       tc_fence_before();
       cluster_sync();  // partial logits and the ticket delivered
       tc_fence_after();
@@ -308,10 +318,8 @@ __global__ void __launch_bounds__(kNT, 2)
       const float lam = fminf(fmaxf(__ldg(p.lam_h + h) + p.gate_scale * (sg - 0.5f), p.gate_lo), p.gate_hi);
       lam_s[tid] = tg >= p.S ? make_float4(1.f, 1.f, 0.f, 0.f) : make_float4(lam, lam, 1.f - lam, 1.f - lam);
     } else {
-      if (tid == 0) tk_s[(i + 2) % 3] = atomicAdd(&p.ws->ticket, 1u);
-      const float lam = p.lam_tok ? (tg < p.S ? __ldg(p.lam_tok + ((size_t)b * p.S + tg) * p.H + h) : 1.f)
-                                  : (p.lam_h ? __ldg(p.lam_h + h) : p.momentum);
-      lam_s[tid] = tg >= p.S ? make_float4(1.f, 1.f, 0.f, 0.f) : make_float4(lam, lam, 1.f - lam, 1.f - lam);
+      if (tid == 0) tk_s[(i + 2) % 3] = t_ahead;
+      lam_s[tid] = tg >= p.S ? make_float4(1.f, 1.f, 0.f, 0.f) : make_float4(lam_in, lam_in, 1.f - lam_in, 1.f - lam_in);
     }
     __syncthreads();
 
@@ -362,12 +370,9 @@ __global__ void __launch_bounds__(kNT, 2)
       }
     }
     __syncthreads();
-    // the CTA's writes are ordered before the flag by the barrier plus a
-    // gpu-scope release fence in the publishing thread
-    if (c > 0 && tid == 0) {
-      __threadfence();
-      st_release(p.lbflag + n, (epoch << 2) | 1u);
-    }
+    // the CTA's writes are ordered before the flag by the barrier and the
+    // gpu-scope release store of the publishing thread
+    if (c > 0 && tid == 32) st_release(p.lbflag + n, (epoch << 2) | 1u);  // warp 1: warp 0 looks back
     if (c > 0 && warp == 0) {
       // warp-wide window: lane i probes chunk (base - i); nearest inclusive wins
       int base = c - 1, kincl = -1;
@@ -417,10 +422,7 @@ __global__ void __launch_bounds__(kNT, 2)
       p.incB[n * kHD + tid] = fmaf(chunkA, X, chunkB);
     }
     __syncthreads();
-    if (tid == 0) {
-      __threadfence();
-      st_release(p.lbflag + n, (epoch << 2) | 2u);
-    }
+    if (tid == 32) st_release(p.lbflag + n, (epoch << 2) | 2u);
 
     // outputs
     {
@@ -531,17 +533,13 @@ cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& mo, Params p, cudaS
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  int units;
-  if (GATE) {
-    int nclusters = 0;
-    cfg.gridDim = dim3(p.H * 64, 1, 1);
-    if ((e = cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg)) != cudaSuccess) return e;
-    units = nclusters > 0 ? nclusters : 1;
-  } else {
-    int per_sm = 0;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kNT, kSmemAlloc)) != cudaSuccess) return e;
-    units = (per_sm > 0 ? per_sm : 1) * nsm;
-  }
+  // Units = resident CTAs per SM x SMs (divided by the cluster size).  Units
+  // that cannot be resident at once simply start later: a unit takes no
+  // ticket before it runs, and it only ever waits on smaller tickets.
+  int per_sm = 0;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kNT, kSmemAlloc)) != cudaSuccess) return e;
+  int units = (per_sm > 0 ? per_sm : 1) * nsm;
+  if (GATE) units = units / p.H > 0 ? units / p.H : 1;
   if ((uint32_t)units > p.nunits) units = (int)p.nunits;
   p.ngrid = (uint32_t)units;
   cfg.gridDim = dim3(units * (GATE ? p.H : 1), 1, 1);
