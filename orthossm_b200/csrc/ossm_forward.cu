@@ -409,8 +409,8 @@ __global__ void __launch_bounds__(kNT, 2) fwd_scan_kernel(const FwdParams p) {
 using namespace ossm;
 
 bool ossm_tc_eligible(const ossm_fwd_args* a);
-int ossm_tc_launch(const ossm_fwd_args* a, char* ws, size_t off_flag, size_t off_aggA, size_t off_aggB,
-                   size_t off_incB, cudaStream_t st);
+size_t ossm_tc_workspace_bytes(const ossm_fwd_args* a);
+int ossm_tc_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
 
 namespace {
 
@@ -463,7 +463,6 @@ FwdLayout fwd_layout(const ossm_fwd_args* a) {
   l.P = a->head_dim / kV;
   l.RUNS = kNT / l.P;
   l.L = l.RUNS * (fwd_precise(a) ? run_len<true>() : run_len<false>());
-  if (ossm_tc_eligible(a)) l.L = 256;  // TMA / tcgen05 path: 256-token chunks
   l.nchunks = (a->S + l.L - 1) / l.L;
   l.N = (size_t)a->B * a->H * l.nchunks;
   size_t off = sizeof(WsHeader);
@@ -476,8 +475,9 @@ FwdLayout fwd_layout(const ossm_fwd_args* a) {
   l.off_incB = off;
   off = align256(off + l.N * a->head_dim * 4);
   l.off_lam = off;
-  if (a->gate_w && !a->lam_tok && !ossm_tc_eligible(a)) off = align256(off + (size_t)a->B * a->S * a->H * 4);
+  if (a->gate_w && !a->lam_tok) off = align256(off + (size_t)a->B * a->S * a->H * 4);
   l.total = off;
+  if (ossm_tc_eligible(a)) l.total = ossm_tc_workspace_bytes(a);  // fast path records
   return l;
 }
 
@@ -570,7 +570,7 @@ extern "C" int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_
   p.incB = reinterpret_cast<float*>(ws + l.off_incB);
   p.nctas = (uint32_t)l.N;
 
-  if (ossm_tc_eligible(a)) return ossm_tc_launch(a, ws, l.off_flag, l.off_aggA, l.off_aggB, l.off_incB, st);
+  if (ossm_tc_eligible(a)) return ossm_tc_launch(a, ws, st);
 
   if (a->gate_w && !a->lam_tok) {
     if (launch_gate(a, reinterpret_cast<float*>(ws + l.off_lam), st) != cudaSuccess) return OSSM_ELAUNCH;

@@ -1,29 +1,30 @@
-// Forward fast path for bf16 activations with head_dim 64 (sm_100a): a
-// persistent, TMA-pipelined kernel with the per-token decay gate on tcgen05
-// tensor cores inside an H-CTA cluster.
+// Forward fast path for bf16 activations, 8 heads x head_dim 64 (sm_100a).
 //
 // Same arithmetic contract as fwd_scan_kernel in ossm_forward.cu (which
 // restates _fused_clenshaw_ema_kernel, sdpc_kernel.py:988-1209); this file only
-// changes how the work is mapped onto the B200.
+// changes how the work is mapped onto the B200:
 //
-// Work item = (batch b, head h, chunk c of 256 tokens).  Items are handed out
-// in ticket order (chunk-major), so every item's predecessors in its (b, h)
-// chain are already owned by running CTAs when it waits on them.  Two CTAs
-// stay resident per SM and loop over items:
+//   work item = (batch b, chunk c of 32 tokens, all 8 heads): eight TMA loads,
+//     one [32 tokens x 64 channels] bf16 box per head (128-byte swizzle), into
+//     a 32 KB [head][token] tile, double-buffered;
+//   schedule = a persistent grid of (CTAs per SM x SMs) units; unit u takes items
+//     u, u+G, u+2G, ... in order (items chunk-major), so an item's predecessor
+//     in its (b, h) chain is always an earlier or concurrent item of a resident
+//     unit;
+//   warp w = head w, lane = 2 channels, 32 tokens per lane:
+//     u = tanh(clamp(gamma y(xn), +-4)) with packed f32x2 Horner, local scan,
+//     then a warp-local decoupled look-back over (value, tag) 64-bit records
+//     (single-copy atomic: no fences, no CTA barrier), outputs;
+//   gate (optional) = per item a [32 tokens x 512] . [512 x 8 heads] product on
+//     the tensor cores (mma.sync m16n8k16, bf16 x exact, weights split into
+//     bf16 hi + lo), each warp over its own head's 64 channels, summed across
+//     warps in shared memory;
+//   bf16 outputs are written into the consumed tile and leave by a TMA store.
 //
-//   * the x tiles of the next two items are in flight by TMA (3D tensor map,
-//     128-byte swizzle) while the current one is computed: double buffer;
-//   * gate (optional): the cluster holds the H heads of one (b, c); the tile is
-//     the A operand of a tcgen05 MMA D[256x16] = X[256x64] . Wsplit[16x64]^T,
-//     Wsplit = this head's gate weights for all H heads as bf16 hi and lo
-//     halves (x is exact in bf16, hi+lo keeps ~16 mantissa bits of W), with
-//     the accumulator in TMEM.  Partial logits go to the owning head's CTA over
-//     distributed shared memory; one cluster barrier per item;
-//   * lane = 2 channels, warp = a run of 32 tokens: u = tanh(gamma y(xn)) in
-//     registers (packed f32x2 Horner), local scan, per-channel run combine,
-//     decoupled look-back (warp-wide window, deterministic forward fold);
-//   * bf16 outputs are written into the consumed x buffer (same swizzle) and
-//     leave by a TMA store; the buffer is refilled once the store has read it.
+// The carry fold order depends on how far back the nearest inclusive record
+// is when an item looks, so results are reproducible to fp32 rounding of the
+// carry, not bitwise; the generic kernel in ossm_forward.cu is bitwise
+// reproducible.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -31,32 +32,27 @@
 #include "ossm_sm100.cuh"
 
 namespace ossm {
-namespace tc {
+namespace fast {
 
 constexpr int kNT = 256;
-constexpr int kHD = 64;      // channels per item (one head)
-constexpr int kL = 256;      // tokens per item
-constexpr int kR = 32;       // tokens per thread (one run per warp)
-constexpr int kRUNS = 8;     // runs per item
-constexpr int kMaxH = 8;
+constexpr int kH = 8;        // heads (one warp each)
+constexpr int kHD = 64;      // channels per head
+constexpr int kD = kH * kHD;
+constexpr int kL = 32;       // tokens per item
+constexpr int kTile = kL * kH * 128;  // 32 KB: row = head*32 + token, 128 B per row
+constexpr int kWRow = 520;            // gate-weight row pitch in bf16 (1040 B: conflict-free ldmatrix)
 
-// shared memory layout (bytes from a 1024-aligned base)
-constexpr int kTile = kL * 128;                        // one [256][128 B] bf16 tile
-constexpr int kOffX = 0;                               // 2 swizzled x / output tiles
-constexpr int kOffW = kOffX + 2 * kTile;               // [16][128 B] swizzled gate weights
-constexpr int kOffAggB = kOffW + 16 * 128;             // [8 runs][64] f32
-constexpr int kOffAggA = kOffAggB + kRUNS * kHD * 4;   // [8] f32
-constexpr int kOffExclA = kOffAggA + 64;               // [8] f32
-constexpr int kOffCarry = kOffExclA + 64;              // [64] f32
-constexpr int kOffLam = kOffCarry + kHD * 4;           // [256] float4 (lam, lam, 1-lam, 1-lam)
-constexpr int kOffPart = kOffLam + kL * 16;            // [2 items][8 src][256] f32 partial logits
-constexpr int kOffCoef = kOffPart + 2 * kMaxH * kL * 4; // [2 items][8][64] f32 coefficients of (b, h)
-constexpr int kOffBar = kOffCoef + 2 * 8 * kHD * 4;    // mbarriers + scalars
-constexpr int kSmemBytes = kOffBar + 128;
-constexpr int kSmemAlloc = kSmemBytes + 1024;          // slack for 1024-byte alignment
+// shared memory (bytes from a 1024-aligned base)
+constexpr int kOffX = 0;                                // 2 tiles
+constexpr int kOffW = kOffX + 2 * kTile;                // [2 hi/lo][8][kWRow] bf16
+constexpr int kOffLam = kOffW + 2 * kH * kWRow * 2;     // [8 heads][32 tokens] float4
+constexpr int kOffPart = kOffLam + kH * kL * 16;        // [8 warps][32 tokens][8] f32
+constexpr int kOffBar = kOffPart + kH * kL * kH * 4;    // mbarriers
+constexpr int kSmemBytes = kOffBar + 64;
+constexpr int kSmemAlloc = kSmemBytes + 1024;
 
 struct Params {
-  int B, S, H, K, nchunks, D;
+  int B, S, K, nchunks;
   const float* coeffs;
   const float* lam_h;
   float momentum;
@@ -69,16 +65,27 @@ struct Params {
   void* out;
   long long osb, oss;
   WsHeader* ws;
-  uint32_t* lbflag;
-  float* aggA;
-  float* aggB;
-  float* incB;
-  uint32_t nunits;  // items (one per cluster with the gate)
-  uint32_t ngrid;   // persistent units in the grid (clusters with the gate, CTAs without)
+  unsigned long long* inc;   // [N][64] (inclusive state | tag)
+  unsigned long long* agg;   // [N][64] (chunk aggregate state | tag)
+  unsigned long long* aggA;  // [N] (chunk decay product | tag)
+  uint32_t nitems;
 };
 
-// Chebyshev -> monomial coefficients, gamma folded in:
-// sum_k c_k T_k(x) = sum_m a_m x^m with T_0..T_7 written out.
+OSSM_DEV unsigned long long pack_rec(float v, uint32_t tag) {
+  return ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+}
+OSSM_DEV void st_rec(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+OSSM_DEV unsigned long long ld_rec(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+OSSM_DEV uint32_t rec_tag(unsigned long long v) { return (uint32_t)(v >> 32); }
+OSSM_DEV float rec_val(unsigned long long v) { return __uint_as_float((uint32_t)v); }
+
+// Chebyshev -> monomial coefficients with gamma folded in (T_0..T_7 written out).
 OSSM_DEV void cheb_to_mono(const float2 (&ck)[8], float gamma, float2 (&a)[8]) {
   const float2 g2 = make_float2(gamma, gamma);
   auto w = [](float v) { return make_float2(v, v); };
@@ -92,185 +99,165 @@ OSSM_DEV void cheb_to_mono(const float2 (&ck)[8], float gamma, float2 (&a)[8]) {
   a[7] = mul2(mul2(w(64.f), ck[7]), g2);
 }
 
-OSSM_DEV uint32_t xs_offset(int row, int lane) {  // this lane's 2 channels of `row`, 128-byte swizzle
-  return row * 128 + ((((lane >> 2) ^ (row & 7))) << 4) + (lane & 3) * 4;
+// byte offset of (token t, head h, 16-byte chunk j) in the tile: each head's
+// [32 x 128 B] box is 128-byte swizzled (chunk ^= row & 7), so 8 consecutive
+// tokens of one head fall in 8 different bank groups
+OSSM_DEV uint32_t tile_off(int t, int h, int j) { return (uint32_t)((h * kL + t) * 128 + ((j ^ (t & 7)) << 4)); }
+
+OSSM_DEV void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+OSSM_DEV void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 template <bool GATE, bool PRECISE, typename OT>
 __global__ void __launch_bounds__(kNT, 2)
-    fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_o,
-                  const Params p) {
+    fwd_fast_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_o,
+                    const Params p) {
   using namespace sm100;
-  constexpr bool kTmaOut = sizeof(OT) == 2;  // bf16 outputs leave by TMA store
+  constexpr bool kTmaOut = sizeof(OT) == 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* wsm = sm + kOffW;
-  float* aggB_s = reinterpret_cast<float*>(sm + kOffAggB);
-  float* aggA_s = reinterpret_cast<float*>(sm + kOffAggA);
-  float* exclA_s = reinterpret_cast<float*>(sm + kOffExclA);
-  float* carry_s = reinterpret_cast<float*>(sm + kOffCarry);
+  __nv_bfloat16* wsm = reinterpret_cast<__nv_bfloat16*>(sm + kOffW);
   float4* lam_s = reinterpret_cast<float4*>(sm + kOffLam);
   float* part_s = reinterpret_cast<float*>(sm + kOffPart);
-  uint64_t* tma_bar = reinterpret_cast<uint64_t*>(sm + kOffBar);  // [2]
-  uint64_t* mma_bar = tma_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffBar + 32);
-  uint32_t* tk_s = tmem_slot + 1;  // [3] ticket ring
-  uint32_t* s_epoch = tmem_slot + 4;
-  int* s_kincl = reinterpret_cast<int*>(tmem_slot + 5);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);  // [2]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const uint32_t crank = GATE ? cluster_rank() : 0u;
-  const bool leader = GATE ? (crank == 0) : true;  // takes the unit's tickets
+  const int h = warp;
+  const int j0 = lane * 2;
+  const int ch0 = h * kHD + j0;
+  const float gamma = 0.98f - 0.06f * (float)h / (float)kH;
+  const uint32_t G = gridDim.x;
+  const uint32_t u = blockIdx.x;
 
-  // ---- prologue ----------------------------------------------------------------
+  const uint32_t epoch = atomicAdd(&p.ws->epoch, 0u);  // advanced only after every unit has left
+  const uint32_t tag_agg = (epoch << 2) | 1u, tag_inc = (epoch << 2) | 2u;
+
+  auto issue_load = [&](uint32_t k, int buf) {
+    const int c = (int)(k / p.B), b = (int)(k % p.B);
+    mbar_expect_tx(bar + buf, kTile);
+#pragma unroll
+    for (int hh = 0; hh < kH; ++hh)
+      tma_load_3d(sm + kOffX + buf * kTile + hh * (kL * 128), &tmap_x, bar + buf, hh * kHD, c * kL, b);
+  };
   if (tid == 0) {
-    mbar_init(tma_bar + 0, 1);
-    mbar_init(tma_bar + 1, 1);
-    mbar_init(mma_bar, 1);
+    mbar_init(bar + 0, 1);
+    mbar_init(bar + 1, 1);
     fence_mbar_init();
     prefetch_tmap(&tmap_x);
     if (kTmaOut) prefetch_tmap(&tmap_o);
-    if (leader) {
-      const uint32_t e = atomicAdd(&p.ws->epoch, 0u);
-      __threadfence();
-      tk_s[0] = atomicAdd(&p.ws->ticket, 1u);
-      tk_s[1] = atomicAdd(&p.ws->ticket, 1u);
-      *s_epoch = e;
-    }
+    if (u < p.nitems) issue_load(u, 0);
+    if (u + G < p.nitems) issue_load(u + G, 1);
   }
-  if (GATE && warp == 1) tmem_alloc(tmem_slot, 32);
   if (GATE) {
-    // gate weights of this CTA's head (the cluster rank), bf16 hi/lo, swizzled
-    const int n = tid >> 4;         // rows 0-7 hi, 8-15 lo
-    const int k0 = (tid & 15) * 4;  // channel within the head
-    const int hh = n & 7;
-    float w[4] = {0.f, 0.f, 0.f, 0.f};
-    if (hh < p.H) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(p.gate_w + (size_t)hh * p.D + crank * kHD + k0));
-      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-    }
-    uint16_t e16[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const __nv_bfloat16 hi = __float2bfloat16_rn(w[q]);
-      const __nv_bfloat16 o = n < 8 ? hi : __float2bfloat16_rn(w[q] - __bfloat162float(hi));
-      e16[q] = *reinterpret_cast<const uint16_t*>(&o);
-    }
-    const int byte = k0 * 2;
-    *reinterpret_cast<uint2*>(wsm + n * 128 + ((((byte >> 4) ^ (n & 7))) << 4) + (byte & 15)) =
-        make_uint2((uint32_t)e16[0] | ((uint32_t)e16[1] << 16), (uint32_t)e16[2] | ((uint32_t)e16[3] << 16));
-    fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-    tc_fence_before();
-    cluster_sync();  // every CTA started (DSMEM addressable); rank 0 holds the first tickets
-    tc_fence_after();
-    if (tid == 0) {
-      tk_s[0] = ld_cluster_u32(map_smem(tk_s + 0, 0));
-      tk_s[1] = ld_cluster_u32(map_smem(tk_s + 1, 0));
-      *s_epoch = ld_cluster_u32(map_smem(s_epoch, 0));
+    // gate weights as bf16 hi / lo, rows = target head, pitch kWRow
+    for (int i = tid; i < kH * kD; i += kNT) {
+      const int n = i / kD, k = i % kD;
+      const float w = __ldg(p.gate_w + (size_t)n * kD + k);
+      const __nv_bfloat16 hi = __float2bfloat16_rn(w);
+      wsm[n * kWRow + k] = hi;
+      wsm[kH * kWRow + n * kWRow + k] = __float2bfloat16_rn(w - __bfloat162float(hi));
     }
   }
   __syncthreads();
-  const uint32_t epoch = *s_epoch;
-  const uint32_t tmem = GATE ? *tmem_slot : 0u;
 
-  auto decode = [&](uint32_t t, int& b, int& h, int& c) {
-    if (GATE) {
-      c = (int)(t / p.B);
-      b = (int)(t % p.B);
-      h = (int)crank;
-    } else {
-      c = (int)(t / (p.B * p.H));
-      const int rem = (int)(t % (p.B * p.H));
-      b = rem / p.H;
-      h = rem % p.H;
-    }
-  };
-  auto issue_load = [&](uint32_t t, int buf) {  // one thread: x tile + the (b, h) coefficients
-    int b, h, c;
-    decode(t, b, h, c);
-    const uint32_t cbytes = (uint32_t)p.K * kHD * 4;
-    mbar_expect_tx(tma_bar + buf, kTile + cbytes);
-    tma_load_3d(sm + kOffX + buf * kTile, &tmap_x, tma_bar + buf, h * kHD, c * kL, b);
-    bulk_load(sm + kOffCoef + buf * (8 * kHD * 4), p.coeffs + ((size_t)(b * p.H + h) * p.K) * kHD, cbytes,
-              tma_bar + buf);
-  };
-  if (tid == 0) {
-    if (tk_s[0] < p.nunits) issue_load(tk_s[0], 0);
-    if (tk_s[1] < p.nunits) issue_load(tk_s[1], 1);
-  }
-
-  const int run = warp;     // tokens run*32 .. run*32+31 of the item
-  const int j0 = lane * 2;  // channel pair within the head
+  float2 cf[8];
+  int cur_b = -1;
   bool ok = true;
+  const uint32_t wbase = smem_u32(wsm);
 
-  // ---- item loop -----------------------------------------------------------------
-  for (int i = 0;; ++i) {
-    const uint32_t T = tk_s[i % 3];
-    if (T >= p.nunits) break;
-    int b, h, c;
-    decode(T, b, h, c);
-    const int buf = i & 1;
+  for (uint32_t k = u, it = 0; k < p.nitems; k += G, ++it) {
+    const int buf = (int)(it & 1u);
     uint8_t* xs = sm + kOffX + buf * kTile;
+    const int c = (int)(k / p.B), b = (int)(k % p.B);
     const int t0 = c * kL;
-    const int ch0 = h * kHD + j0;
-    const float gamma = 0.98f - 0.06f * (float)h / (float)p.H;
 
-    // the ticket two items ahead: issued now, consumed after the evaluation
-    uint32_t t_ahead = 0;
-    if (tid == 0 && leader) t_ahead = atomicAdd(&p.ws->ticket, 1u);
-    // per-token decay supplied by the caller: load early as well
-    const int tg = t0 + tid;
-    float lam_in = 1.f;
-    if (!GATE) {
-      lam_in = p.lam_tok ? (tg < p.S ? __ldg(p.lam_tok + ((size_t)b * p.S + tg) * p.H + h) : 1.f)
-                         : (p.lam_h ? __ldg(p.lam_h + h) : p.momentum);
-    }
-
-    ok &= mbar_wait(tma_bar + buf, (uint32_t)(i >> 1) & 1u);
-
-    // coefficients of (b, h) from the tile's transaction: raw Chebyshev
-    // (precise) or gamma-folded monomial
-    float2 cf[8];
-    {
-      const float* cs = reinterpret_cast<const float*>(sm + kOffCoef + buf * (8 * kHD * 4)) + j0;
+    if (b != cur_b) {  // coefficients of (b, h): raw (precise) or gamma-folded monomial
+      cur_b = b;
+      const float* cb = p.coeffs + ((size_t)(b * kH + h) * p.K) * kHD + j0;
       float2 ck[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) ck[k] = k < p.K ? *reinterpret_cast<const float2*>(cs + k * kHD) : make_float2(0.f, 0.f);
+      for (int q = 0; q < 8; ++q)
+        ck[q] = q < p.K ? __ldg(reinterpret_cast<const float2*>(cb + q * kHD)) : make_float2(0.f, 0.f);
       if (PRECISE) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) cf[k] = ck[k];
+        for (int q = 0; q < 8; ++q) cf[q] = ck[q];
       } else {
         cheb_to_mono(ck, gamma, cf);
       }
     }
-
-    // gate MMA (one thread): D[tokens][16] in TMEM
-    if (GATE && tid == 0) {
-      tc_fence_after();
-      constexpr uint32_t idesc = umma_idesc_bf16(128, 16);
-      const uint32_t xa = smem_u32(xs), wa = smem_u32(wsm);
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          umma_bf16(tmem + mt * 16, umma_desc_sw128(xa + mt * 128 * 128 + ks * 32), umma_desc_sw128(wa + ks * 32),
-                    idesc, ks > 0 ? 1u : 0u);
-      umma_commit(mma_bar);
+    float lam_in = 1.f;  // caller's per-token decay for token (t0 + lane), head h
+    if (!GATE) {
+      const int tg = t0 + lane;
+      lam_in = p.lam_tok ? (tg < p.S ? __ldg(p.lam_tok + ((size_t)b * p.S + tg) * kH + h) : 1.f)
+                         : (p.lam_h ? __ldg(p.lam_h + h) : p.momentum);
     }
 
-    // u = tanh(clamp(gamma y(xn), +-4)) into registers
-    float2 sl[kR];
+    ok &= mbar_wait(bar + buf, (it >> 1) & 1u);
+    const uint32_t xa = smem_u32(xs);
+
+    // ---- gate: partial logits of this head's 64 channels on the tensor cores ----
+    if (GATE) {
+      const int m = lane >> 3, rr = lane & 7;
 #pragma unroll
-    for (int r = 0; r < kR; ++r) {
-      const int row = run * kR + r;
-      const uint32_t raw = *reinterpret_cast<const uint32_t*>(xs + xs_offset(row, lane));
+      for (int mt = 0; mt < 2; ++mt) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          uint32_t a[4], bw[4];
+          // A: tokens mt*16 + (m&1)*8 + rr, channels ks*16 + (m>>1)*8 of head h
+          ldmatrix_x4(xa + tile_off(mt * 16 + (m & 1) * 8 + rr, h, ks * 2 + (m >> 1)), a);
+          // B: weight rows n = rr, channels h*64 + ks*16 + (m&1)*8; lanes 0-15 hi, 16-31 lo
+          const int kk = h * kHD + ks * 16 + (m & 1) * 8;
+          ldmatrix_x4(wbase + (uint32_t)(((m >> 1) * kH * kWRow + rr * kWRow + kk) * 2), bw);
+          mma_bf16_16816(d, a, bw[0], bw[1]);
+          mma_bf16_16816(d, a, bw[2], bw[3]);
+        }
+        const int gid = lane >> 2, tig = lane & 3;
+        float* pw = part_s + h * (kL * kH);
+        pw[(mt * 16 + gid) * kH + 2 * tig] = d[0];
+        pw[(mt * 16 + gid) * kH + 2 * tig + 1] = d[1];
+        pw[(mt * 16 + gid + 8) * kH + 2 * tig] = d[2];
+        pw[(mt * 16 + gid + 8) * kH + 2 * tig + 1] = d[3];
+      }
+      __syncthreads();
+      {
+        const int t = tid >> 3, n = tid & 7;
+        float logit = __ldg(p.gate_b + n);
+#pragma unroll
+        for (int g = 0; g < kH; ++g) logit += part_s[g * (kL * kH) + t * kH + n];
+        const float sg = 1.0f / (1.0f + __expf(-logit));
+        const float lam = fminf(fmaxf(__ldg(p.lam_h + n) + p.gate_scale * (sg - 0.5f), p.gate_lo), p.gate_hi);
+        lam_s[n * kL + t] =
+            (t0 + t) < p.S ? make_float4(lam, lam, 1.f - lam, 1.f - lam) : make_float4(1.f, 1.f, 0.f, 0.f);
+      }
+      __syncthreads();
+    } else {
+      lam_s[h * kL + lane] = (t0 + lane) < p.S ? make_float4(lam_in, lam_in, 1.f - lam_in, 1.f - lam_in)
+                                               : make_float4(1.f, 1.f, 0.f, 0.f);
+      __syncwarp();
+    }
+
+    // ---- u for 32 tokens, local scan ----------------------------------------------
+    float2 sl[kL];
+#pragma unroll
+    for (int t = 0; t < kL; ++t) {
+      const uint32_t raw = *reinterpret_cast<const uint32_t*>(xs + tile_off(t, h, lane >> 2) + (lane & 3) * 4);
       const float x0 = __uint_as_float(raw << 16), x1 = __uint_as_float(raw & 0xffff0000u);
       float2 xn;
       if (PRECISE) {
-        float xa, sg;
-        xn.x = softsign<true>(x0, false, xa, sg);
-        xn.y = softsign<true>(x1, false, xa, sg);
+        float xa_, sg;
+        xn.x = softsign<true>(x0, false, xa_, sg);
+        xn.y = softsign<true>(x1, false, xa_, sg);
       } else {
         xn = make_float2(x0 * rcp_fast(1.0f + fabsf(x0)), x1 * rcp_fast(1.0f + fabsf(x1)));  // x / (1 + |x|)
       }
@@ -279,207 +266,123 @@ __global__ void __launch_bounds__(kNT, 2)
         const float2 x2 = make_float2(2.f * xn.x, 2.f * xn.y);
         float2 u1 = cf[7], u2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int k = 6; k >= 1; --k) {
-          const float2 t = fma2(x2, u1, sub2(cf[k], u2));
+        for (int q = 6; q >= 1; --q) {
+          const float2 tt = fma2(x2, u1, sub2(cf[q], u2));
           u2 = u1;
-          u1 = t;
+          u1 = tt;
         }
         y = fma2(xn, u1, sub2(cf[0], u2));
         y = make_float2(y.x * gamma, y.y * gamma);
       } else {
         y = cf[7];
 #pragma unroll
-        for (int m = 6; m >= 0; --m) y = fma2(y, xn, cf[m]);
+        for (int q = 6; q >= 0; --q) y = fma2(y, xn, cf[q]);
       }
       const float z0 = fminf(fmaxf(y.x, -4.f), 4.f), z1 = fminf(fmaxf(y.y, -4.f), 4.f);
       const float u0 = PRECISE ? tanhf(z0) : tanh_fast(z0);
       const float u1v = PRECISE ? tanhf(z1) : tanh_fast(z1);
-      sl[r] = make_float2(x0 == x0 ? u0 : 0.f, x1 == x1 ? u1v : 0.f);  // NaN input -> 0 (sdpc_kernel.py:1164)
+      sl[t] = make_float2(x0 == x0 ? u0 : 0.f, x1 == x1 ? u1v : 0.f);  // NaN input -> 0 (sdpc_kernel.py:1164)
+    }
+    float2 s2 = make_float2(0.f, 0.f);
+    float A = 1.f;
+#pragma unroll
+    for (int t = 0; t < kL; ++t) {
+      const float4 lm = lam_s[h * kL + t];
+      if (t0 + t == 0) {
+        // first token of the sequence: fold the carried-in state with its clamp
+        const float2 iv = p.init ? __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + ch0))
+                                 : make_float2(0.f, 0.f);
+        s2 = make_float2(clamp1(fmaf(lm.x, iv.x, lm.z * sl[t].x)), clamp1(fmaf(lm.x, iv.y, lm.z * sl[t].y)));
+        A = 0.f;
+      } else {
+        s2 = fma2(make_float2(lm.x, lm.y), s2, mul2(make_float2(lm.z, lm.w), sl[t]));
+        A *= lm.x;
+      }
+      sl[t] = s2;
     }
 
-    // decay of each token; publish the ticket taken above
-    if (GATE) {
-      ok &= mbar_wait(mma_bar, (uint32_t)i & 1u);
-      tc_fence_after();
-      const int q4 = warp & 3, mt = warp >> 2;
-      float v[16];
-      tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + mt * 16, v);
-      const int tok = mt * 128 + q4 * 32 + lane;
-      float* part_i = part_s + buf * (kMaxH * kL);
-      for (int n = 0; n < p.H; ++n) st_cluster_f32(map_smem(part_i + crank * kL + tok, n), v[n] + v[n + 8]);
-      if (tid == 0 && leader)
-        for (int r = 0; r < p.H; ++r) st_cluster_u32(map_smem(tk_s + (i + 2) % 3, r), t_ahead);
-      tc_fence_before();
-      cluster_sync();  // partial logits and the ticket delivered
-      tc_fence_after();
-      float logit = __ldg(p.gate_b + h);
-      for (int s = 0; s < p.H; ++s) logit += part_i[s * kL + tid];
-      const float sg = 1.0f / (1.0f + __expf(-logit));
-      const float lam = fminf(fmaxf(__ldg(p.lam_h + h) + p.gate_scale * (sg - 0.5f), p.gate_lo), p.gate_hi);
-      lam_s[tid] = tg >= p.S ? make_float4(1.f, 1.f, 0.f, 0.f) : make_float4(lam, lam, 1.f - lam, 1.f - lam);
+    // ---- publish the aggregate, look back, publish the inclusive state -----------
+    const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
+    float2 X = make_float2(0.f, 0.f);
+    if (c == 0) {
+      st_rec(p.inc + n * kHD + j0, pack_rec(s2.x, tag_inc));
+      st_rec(p.inc + n * kHD + j0 + 1, pack_rec(s2.y, tag_inc));
     } else {
-      if (tid == 0) tk_s[(i + 2) % 3] = t_ahead;
-      lam_s[tid] = tg >= p.S ? make_float4(1.f, 1.f, 0.f, 0.f) : make_float4(lam_in, lam_in, 1.f - lam_in, 1.f - lam_in);
-    }
-    __syncthreads();
-
-    // local scan of each run
-    const int tbase = t0 + run * kR;
-    {
-      float2 s2 = make_float2(0.f, 0.f);
-      float Arun = 1.f;
-#pragma unroll
-      for (int r = 0; r < kR; ++r) {
-        const float4 lm = lam_s[run * kR + r];
-        if (tbase + r == 0) {
-          // first token of the sequence: fold the carried-in state with its clamp
-          const float2 iv = p.init ? __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * p.D + ch0))
-                                   : make_float2(0.f, 0.f);
-          s2 = make_float2(clamp1(fmaf(lm.x, iv.x, lm.z * sl[r].x)), clamp1(fmaf(lm.x, iv.y, lm.z * sl[r].y)));
-          Arun = 0.f;
-        } else {
-          s2 = fma2(make_float2(lm.x, lm.y), s2, mul2(make_float2(lm.z, lm.w), sl[r]));
-          Arun *= lm.x;
-        }
-        sl[r] = s2;
-      }
-      *reinterpret_cast<float2*>(aggB_s + run * kHD + j0) = s2;
-      if (lane == 0) aggA_s[run] = Arun;
-    }
-    __syncthreads();
-
-    // combine runs per channel, publish the chunk aggregate
-    const size_t n = (size_t)(b * p.H + h) * p.nchunks + c;
-    float chunkB = 0.f, chunkA = 1.f;
-    if (tid < kHD) {
-      float Bv = 0.f, Av = 1.f;
-#pragma unroll
-      for (int q = 0; q < kRUNS; ++q) {
-        const float aq = aggA_s[q];
-        const float bq = aggB_s[q * kHD + tid];
-        aggB_s[q * kHD + tid] = Bv;
-        if (tid == 0) exclA_s[q] = Av;
-        Bv = fmaf(aq, Bv, bq);
-        Av *= aq;
-      }
-      chunkB = Bv;
-      chunkA = Av;
-      if (c > 0) {
-        p.aggB[n * kHD + tid] = chunkB;
-        if (tid == 0) p.aggA[n] = chunkA;
-      }
-    }
-    __syncthreads();
-    // the CTA's writes are ordered before the flag by the barrier and the
-    // gpu-scope release store of the publishing thread
-    if (c > 0 && tid == 32) st_release(p.lbflag + n, (epoch << 2) | 1u);  // warp 1: warp 0 looks back
-    if (c > 0 && warp == 0) {
-      // warp-wide window: lane i probes chunk (base - i); nearest inclusive wins
-      int base = c - 1, kincl = -1;
-      bool okw = true;
-      while (kincl < 0) {
-        const int j = base - lane;
-        uint32_t st = 0;
-        if (j >= 0) st = wait_flag(p.lbflag + (n - (size_t)(c - j)), epoch);
-        if (__ballot_sync(0xffffffffu, j >= 0 && st == 0)) {
-          okw = false;
+      st_rec(p.agg + n * kHD + j0, pack_rec(s2.x, tag_agg));
+      st_rec(p.agg + n * kHD + j0 + 1, pack_rec(s2.y, tag_agg));
+      if (lane == 0) st_rec(p.aggA + n, pack_rec(A, tag_agg));
+      float2 accB = make_float2(0.f, 0.f);
+      float accA = 1.f;
+      size_t nj = n - 1;
+      uint32_t spins = 0;
+      while (true) {
+        const unsigned long long i0 = ld_rec(p.inc + nj * kHD + j0);
+        const unsigned long long i1 = ld_rec(p.inc + nj * kHD + j0 + 1);
+        const unsigned long long a0 = ld_rec(p.agg + nj * kHD + j0);
+        const unsigned long long a1 = ld_rec(p.agg + nj * kHD + j0 + 1);
+        const unsigned long long aa = ld_rec(p.aggA + nj);
+        if (rec_tag(i0) == tag_inc && rec_tag(i1) == tag_inc) {
+          X = make_float2(fmaf(accA, rec_val(i0), accB.x), fmaf(accA, rec_val(i1), accB.y));
           break;
         }
-        const uint32_t m2 = __ballot_sync(0xffffffffu, j >= 0 && st == 2);
-        if (m2) kincl = base - (__ffs(m2) - 1);
-        else base -= 32;
-      }
-      if (lane == 0) *s_kincl = okw ? kincl : -1;
-    }
-    __syncthreads();
-    if (tid < kHD) {
-      float X = 0.f;
-      if (c > 0) {
-        const int k = *s_kincl;
-        if (k >= 0) {
-          X = __ldcg(p.incB + (n - (size_t)(c - k)) * kHD + tid);
-          int j = k + 1;  // fold forward 4 chunks at a time; loads do not depend on X
-          for (; j + 4 <= c; j += 4) {
-            float aa[4], bb[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const size_t nj = n - (size_t)(c - (j + u));
-              aa[u] = __ldcg(p.aggA + nj);
-              bb[u] = __ldcg(p.aggB + nj * kHD + tid);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) X = fmaf(aa[u], X, bb[u]);
-          }
-          for (; j < c; ++j) {
-            const size_t nj = n - (size_t)(c - j);
-            X = fmaf(__ldcg(p.aggA + nj), X, __ldcg(p.aggB + nj * kHD + tid));
-          }
-        } else {
+        if (rec_tag(a0) == tag_agg && rec_tag(a1) == tag_agg && rec_tag(aa) == tag_agg) {
+          accB = make_float2(fmaf(accA, rec_val(a0), accB.x), fmaf(accA, rec_val(a1), accB.y));
+          accA *= rec_val(aa);
+          --nj;  // chunk 0 always publishes an inclusive record, so the walk stays in the chain
+          continue;
+        }
+        if (++spins > kSpinLimit) {
           ok = false;
+          break;
         }
+        if (spins > 16) __nanosleep(64);
       }
-      carry_s[tid] = X;
-      p.incB[n * kHD + tid] = fmaf(chunkA, X, chunkB);
+      st_rec(p.inc + n * kHD + j0, pack_rec(fmaf(A, X.x, s2.x), tag_inc));
+      st_rec(p.inc + n * kHD + j0 + 1, pack_rec(fmaf(A, X.y, s2.y), tag_inc));
     }
-    __syncthreads();
-    if (tid == 32) st_release(p.lbflag + n, (epoch << 2) | 2u);
 
-    // outputs
-    {
-      const float ea = exclA_s[run];
-      const float2 cv = *reinterpret_cast<const float2*>(carry_s + j0);
-      const float2 eb = *reinterpret_cast<const float2*>(aggB_s + run * kHD + j0);
-      const float2 rc = make_float2(fmaf(ea, cv.x, eb.x), fmaf(ea, cv.y, eb.y));
-      OT* ob = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + ch0;
-      float2 A2 = make_float2(1.f, 1.f);
+    // ---- outputs ----------------------------------------------------------------------
+    OT* ob = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + ch0;
+    float2 A2 = make_float2(1.f, 1.f);
 #pragma unroll
-      for (int r = 0; r < kR; ++r) {
-        const int t = tbase + r;
-        const int row = run * kR + r;
-        const float4 lm = lam_s[row];
-        A2 = mul2(A2, make_float2(lm.x, lm.y));
-        float2 o = fma2(A2, rc, sl[r]);
-        if (kTmaOut) {
-          *reinterpret_cast<uint32_t*>(xs + xs_offset(row, lane)) = pack_bf16x2(o.x, o.y);
-        } else {
-          o = make_float2(clamp1(o.x), clamp1(o.y));
-          if (t < p.S) st2(ob + (size_t)t * p.oss, o);
-        }
-        if (t == p.S - 1 && p.fin)
-          *reinterpret_cast<float2*>(p.fin + (size_t)b * p.D + ch0) = make_float2(clamp1(o.x), clamp1(o.y));
+    for (int t = 0; t < kL; ++t) {
+      const float4 lm = lam_s[h * kL + t];
+      A2 = mul2(A2, make_float2(lm.x, lm.y));
+      float2 o = fma2(A2, X, sl[t]);
+      const int tg = t0 + t;
+      if (kTmaOut) {
+        *reinterpret_cast<uint32_t*>(xs + tile_off(t, h, lane >> 2) + (lane & 3) * 4) = pack_bf16x2(o.x, o.y);
+      } else {
+        o = make_float2(clamp1(o.x), clamp1(o.y));
+        if (tg < p.S) st2(ob + (size_t)tg * p.oss, o);
       }
-      if (kTmaOut) fence_proxy_async_smem();
+      if (tg == p.S - 1 && p.fin)
+        *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) = make_float2(clamp1(o.x), clamp1(o.y));
     }
-    __syncthreads();
+    if (kTmaOut) fence_proxy_async_smem();
+    __syncthreads();  // tile complete; lam_s / part_s free for the next item
     if (tid == 0) {
       if (kTmaOut) {
-        tma_store_3d(&tmap_o, xs, h * kHD, t0, b);
+#pragma unroll
+        for (int hh = 0; hh < kH; ++hh) tma_store_3d(&tmap_o, xs + hh * (kL * 128), hh * kHD, t0, b);
         bulk_commit();
       }
-      const uint32_t t2 = tk_s[(i + 2) % 3];
-      if (t2 < p.nunits) {
-        if (kTmaOut) bulk_wait_read0();  // the store has read the buffer
-        issue_load(t2, buf);
+      if (k + 2 * G < p.nitems) {
+        if (kTmaOut) bulk_wait_read0();  // the store has read this tile
+        issue_load(k + 2 * G, buf);
       }
     }
   }
 
-  // ---- epilogue ------------------------------------------------------------------
   if (tid == 0 && kTmaOut) bulk_wait0();
   if (!ok) {
     atomicExch(&p.ws->status, (uint32_t)OSSM_ETIMEOUT);
     atomicAdd(&p.ws->timeouts, 1u);
   }
-  if (GATE) {
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) tmem_dealloc(tmem, 32);
-  }
-  if (tid == 0 && leader) {
-    // the last unit to leave resets the ticket counter and advances the epoch
+  if (tid == 0) {
+    // the last unit to leave advances the epoch that tags the records
     __threadfence();
-    if (atomicAdd(&p.ws->exited, 1u) == p.ngrid - 1) {
-      atomicExch(&p.ws->ticket, 0u);
+    if (atomicAdd(&p.ws->exited, 1u) == G - 1) {
       atomicExch(&p.ws->exited, 0u);
       atomicExch(&p.ws->epoch, epoch + 1u);
     }
@@ -502,9 +405,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [B, S, D] bf16 tensor as a 3D map with a [1, 256, 64] box (128-byte swizzle).
-bool encode_tile_map(CUtensorMap* map, const void* base, int D, int S, int B, long long ss, long long sb) {
-  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)B};
+// [B, S, 512] bf16 as a 3D map with a [1, 32, 64] box (one head), 128-byte swizzle.
+bool encode_map(CUtensorMap* map, const void* base, int S, int B, long long ss, long long sb) {
+  cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)S, (cuuint64_t)B};
   const long long sbb = B > 1 ? sb : (long long)S * ss;
   cuuint64_t strides[2] = {(cuuint64_t)ss * 2, (cuuint64_t)sbb * 2};
   cuuint32_t box[3] = {(cuuint32_t)kHD, (cuuint32_t)kL, 1};
@@ -515,67 +418,52 @@ bool encode_tile_map(CUtensorMap* map, const void* base, int D, int S, int B, lo
 }
 
 template <bool GATE, bool PRECISE, typename OT>
-cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& mo, Params p, cudaStream_t st) {
-  auto kern = fwd_tc_kernel<GATE, PRECISE, OT>;
+cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& mo, const Params& p, cudaStream_t st) {
+  auto kern = fwd_fast_kernel<GATE, PRECISE, OT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
   if (e != cudaSuccess) return e;
-  int dev = 0, nsm = 0;
+  int dev = 0, nsm = 0, per_sm = 0;
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
   if ((e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(kNT, 1, 1);
-  cfg.dynamicSmemBytes = kSmemAlloc;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = GATE ? p.H : 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  // Units = resident CTAs per SM x SMs (divided by the cluster size).  Units
-  // that cannot be resident at once simply start later: a unit takes no
-  // ticket before it runs, and it only ever waits on smaller tickets.
-  int per_sm = 0;
   if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kNT, kSmemAlloc)) != cudaSuccess) return e;
-  int units = (per_sm > 0 ? per_sm : 1) * nsm;
-  if (GATE) units = units / p.H > 0 ? units / p.H : 1;
-  if ((uint32_t)units > p.nunits) units = (int)p.nunits;
-  p.ngrid = (uint32_t)units;
-  cfg.gridDim = dim3(units * (GATE ? p.H : 1), 1, 1);
-  return cudaLaunchKernelEx(&cfg, kern, mx, mo, p);
+  // every unit must be resident at once (a unit waits on items of other units)
+  uint32_t G = (uint32_t)((per_sm > 0 ? per_sm : 1) * nsm);
+  if (G > p.nitems) G = p.nitems;
+  kern<<<G, kNT, kSmemAlloc, st>>>(mx, mo, p);
+  return cudaGetLastError();
 }
 
-}  // namespace tc
+}  // namespace fast
 }  // namespace ossm
 
 using namespace ossm;
 
-// Eligibility of the TMA / tcgen05 path for these arguments.
 bool ossm_tc_eligible(const ossm_fwd_args* a) {
-  if (a->x_dtype != OSSM_BF16 || a->head_dim != 64 || a->tanh_out) return false;
+  if (a->x_dtype != OSSM_BF16 || a->H != fast::kH || a->head_dim != fast::kHD || a->tanh_out) return false;
   if ((a->flags & OSSM_EVAL_MASK) == OSSM_EVAL_LUT || (a->flags & (OSSM_F_FASTPATH | OSSM_F_GENERIC))) return false;
   if (((uintptr_t)a->x % 16) || (a->x_stride_s % 8) || (a->B > 1 && (a->x_stride_b % 8))) return false;
   if (a->out_dtype == OSSM_BF16 &&
       (((uintptr_t)a->out % 16) || (a->out_stride_s % 8) || (a->B > 1 && (a->out_stride_b % 8))))
     return false;
-  if (a->gate_w && !a->lam_tok && a->H > tc::kMaxH) return false;
   if (a->S > (1 << 30)) return false;
-  return tc::encode_fn() != nullptr;
+  return fast::encode_fn() != nullptr;
 }
 
-// Launch of the TMA / tcgen05 path (same workspace layout as the generic path:
-// header, flags[N], aggA[N], aggB[N][64], incB[N][64] with N = B*H*nchunks).
-int ossm_tc_launch(const ossm_fwd_args* a, char* ws, size_t off_flag, size_t off_aggA, size_t off_aggB,
-                   size_t off_incB, cudaStream_t st) {
-  using namespace tc;
+// Workspace of the fast path: header, then inclusive / aggregate records.
+size_t ossm_tc_workspace_bytes(const ossm_fwd_args* a) {
+  const size_t nch = (size_t)(a->S + fast::kL - 1) / fast::kL;
+  const size_t N = (size_t)a->B * fast::kH * nch;
+  auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+  return al(sizeof(WsHeader)) + 2 * al(N * fast::kHD * 8) + al(N * 8);
+}
+
+int ossm_tc_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
+  using namespace fast;
   Params p;
   p.B = a->B;
   p.S = a->S;
-  p.H = a->H;
   p.K = a->degree;
   p.nchunks = (a->S + kL - 1) / kL;
-  p.D = a->H * kHD;
   p.coeffs = a->coeffs;
   p.lam_h = a->lam_h;
   p.momentum = a->momentum;
@@ -591,20 +479,23 @@ int ossm_tc_launch(const ossm_fwd_args* a, char* ws, size_t off_flag, size_t off
   p.out = a->out;
   p.osb = a->out_stride_b;
   p.oss = a->out_stride_s;
+  const size_t N = (size_t)a->B * kH * p.nchunks;
+  auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
   p.ws = reinterpret_cast<WsHeader*>(ws);
-  p.lbflag = reinterpret_cast<uint32_t*>(ws + off_flag);
-  p.aggA = reinterpret_cast<float*>(ws + off_aggA);
-  p.aggB = reinterpret_cast<float*>(ws + off_aggB);
-  p.incB = reinterpret_cast<float*>(ws + off_incB);
-  const long long items = (long long)a->B * a->H * p.nchunks;
+  size_t off = al(sizeof(WsHeader));
+  p.inc = reinterpret_cast<unsigned long long*>(ws + off);
+  off += al(N * kHD * 8);
+  p.agg = reinterpret_cast<unsigned long long*>(ws + off);
+  off += al(N * kHD * 8);
+  p.aggA = reinterpret_cast<unsigned long long*>(ws + off);
+  const long long items = (long long)a->B * p.nchunks;
   if (items > 0x7fffffffLL) return OSSM_EINVAL;
-  p.nunits = (uint32_t)(gate ? (long long)a->B * p.nchunks : items);
-  p.ngrid = 0;
+  p.nitems = (uint32_t)items;
 
   CUtensorMap mx, mo;
-  if (!encode_tile_map(&mx, a->x, p.D, a->S, a->B, a->x_stride_s, a->x_stride_b)) return OSSM_EINVAL;
-  mo = mx;  // unused unless the output is bf16
-  if (a->out_dtype == OSSM_BF16 && !encode_tile_map(&mo, a->out, p.D, a->S, a->B, a->out_stride_s, a->out_stride_b))
+  if (!encode_map(&mx, a->x, a->S, a->B, a->x_stride_s, a->x_stride_b)) return OSSM_EINVAL;
+  mo = mx;
+  if (a->out_dtype == OSSM_BF16 && !encode_map(&mo, a->out, a->S, a->B, a->out_stride_s, a->out_stride_b))
     return OSSM_EINVAL;
   const bool precise = (a->out_dtype == OSSM_F32) || (a->flags & OSSM_F_PRECISE);
   cudaError_t e;

@@ -190,15 +190,24 @@ def test_long_chain_lookback():
     assert O.workspace_status() == 0
 
 
-def test_deterministic_and_workspace_reuse():
+@pytest.mark.parametrize("generic", [True, False])
+def test_deterministic_and_workspace_reuse(generic):
+    """The generic kernel is bitwise reproducible; the TMA fast path folds the
+    carry in a timing-dependent order, so it is reproducible to fp32 rounding
+    of the carry (bf16 outputs then differ by at most one bf16 ulp)."""
     x, c, W, b, init = _cfg2_like(4, 8192, seed=80)
-    kw = dict(lambda_per_head=R.BASELINE_LAMBDA, gate_weight=T(W), gate_bias=T(b), init_state=T(init))
+    kw = dict(lambda_per_head=R.BASELINE_LAMBDA, gate_weight=T(W), gate_bias=T(b), init_state=T(init),
+              force_generic=generic)
     xb = T(x, torch.bfloat16)
     o1, f1 = run(xb, T(c), **kw)
     # a different shape in between reuses (and grows) the same workspace
     run(T(det_normal((1, 333, 64), 81)), T(spectral_coeffs(1, 8, 8, 8, 82)))
     o2, f2 = run(xb, T(c), **kw)
-    assert torch.equal(o1, o2) and torch.equal(f1, f2)
+    if generic:
+        assert torch.equal(o1, o2) and torch.equal(f1, f2)
+    else:
+        assert (o1.float() - o2.float()).abs().max().item() <= 2 ** -7
+        assert relerr(N(f1), N(f2)) < 1e-5
 
 
 def test_streaming_chunks_equal_single_call():
