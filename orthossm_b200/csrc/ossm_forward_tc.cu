@@ -173,6 +173,7 @@ __global__ void __launch_bounds__(kNT, 2)
   float2 cf[8];
   int cur_b = -1;
   bool ok = true;
+  uint32_t pend_k = 0xffffffffu;  // item whose tile the previous iteration left to load
   const uint32_t wbase = smem_u32(wsm);
 
   for (uint32_t k = u, it = 0; k < p.nitems; k += G, ++it) {
@@ -283,21 +284,32 @@ __global__ void __launch_bounds__(kNT, 2)
       const float u1v = PRECISE ? tanhf(z1) : tanh_fast(z1);
       sl[t] = make_float2(x0 == x0 ? u0 : 0.f, x1 == x1 ? u1v : 0.f);  // NaN input -> 0 (sdpc_kernel.py:1164)
     }
-    float2 s2 = make_float2(0.f, 0.f);
-    float A = 1.f;
-#pragma unroll
-    for (int t = 0; t < kL; ++t) {
-      const float4 lm = lam_s[h * kL + t];
-      if (t0 + t == 0) {
-        // first token of the sequence: fold the carried-in state with its clamp
+    // the next tile into the other buffer, once the previous item's store has read it
+    if (tid == 0 && pend_k < p.nitems) {
+      if (kTmaOut) bulk_wait_read0();
+      issue_load(pend_k, buf ^ 1);
+    }
+    // local scan: token 0 of the sequence folds the carried-in state (with its clamp)
+    float2 s2;
+    float A;
+    {
+      const float4 lm = lam_s[h * kL];
+      if (t0 == 0) {
         const float2 iv = p.init ? __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + ch0))
                                  : make_float2(0.f, 0.f);
-        s2 = make_float2(clamp1(fmaf(lm.x, iv.x, lm.z * sl[t].x)), clamp1(fmaf(lm.x, iv.y, lm.z * sl[t].y)));
+        s2 = make_float2(clamp1(fmaf(lm.x, iv.x, lm.z * sl[0].x)), clamp1(fmaf(lm.x, iv.y, lm.z * sl[0].y)));
         A = 0.f;
       } else {
-        s2 = fma2(make_float2(lm.x, lm.y), s2, mul2(make_float2(lm.z, lm.w), sl[t]));
-        A *= lm.x;
+        s2 = mul2(make_float2(lm.z, lm.w), sl[0]);
+        A = lm.x;
       }
+      sl[0] = s2;
+    }
+#pragma unroll
+    for (int t = 1; t < kL; ++t) {
+      const float4 lm = lam_s[h * kL + t];
+      s2 = fma2(make_float2(lm.x, lm.y), s2, mul2(make_float2(lm.z, lm.w), sl[t]));
+      A *= lm.x;
       sl[t] = s2;
     }
 
@@ -342,36 +354,44 @@ __global__ void __launch_bounds__(kNT, 2)
     }
 
     // ---- outputs ----------------------------------------------------------------------
-    OT* ob = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + ch0;
-    float2 A2 = make_float2(1.f, 1.f);
+    {
+      float2 A2 = make_float2(1.f, 1.f);
+      if (kTmaOut) {  // into the consumed tile; the TMA store clips rows past S
 #pragma unroll
-    for (int t = 0; t < kL; ++t) {
-      const float4 lm = lam_s[h * kL + t];
-      A2 = mul2(A2, make_float2(lm.x, lm.y));
-      float2 o = fma2(A2, X, sl[t]);
-      const int tg = t0 + t;
-      if (kTmaOut) {
-        *reinterpret_cast<uint32_t*>(xs + tile_off(t, h, lane >> 2) + (lane & 3) * 4) = pack_bf16x2(o.x, o.y);
+        for (int t = 0; t < kL; ++t) {
+          A2 = mul2(A2, make_float2(lam_s[h * kL + t].x, lam_s[h * kL + t].x));
+          const float2 o = fma2(A2, X, sl[t]);
+          *reinterpret_cast<uint32_t*>(xs + tile_off(t, h, lane >> 2) + (lane & 3) * 4) = pack_bf16x2(o.x, o.y);
+        }
       } else {
-        o = make_float2(clamp1(o.x), clamp1(o.y));
-        if (tg < p.S) st2(ob + (size_t)tg * p.oss, o);
+        OT* ob = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + (size_t)t0 * p.oss + ch0;
+        const int nt = min(kL, p.S - t0);
+#pragma unroll
+        for (int t = 0; t < kL; ++t) {
+          A2 = mul2(A2, make_float2(lam_s[h * kL + t].x, lam_s[h * kL + t].x));
+          const float2 o = fma2(A2, X, sl[t]);
+          if (t < nt) st2(ob + (size_t)t * p.oss, make_float2(clamp1(o.x), clamp1(o.y)));
+        }
       }
-      if (tg == p.S - 1 && p.fin)
-        *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) = make_float2(clamp1(o.x), clamp1(o.y));
+      const int tl = p.S - 1 - t0;  // the sequence's last token falls in this item: final state
+      if (p.fin && tl < kL) {
+        float2 B2 = make_float2(1.f, 1.f), v = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int t = 0; t < kL; ++t) {
+          B2 = mul2(B2, make_float2(lam_s[h * kL + t].x, lam_s[h * kL + t].x));
+          if (t == tl) v = fma2(B2, X, sl[t]);
+        }
+        *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) = make_float2(clamp1(v.x), clamp1(v.y));
+      }
     }
     if (kTmaOut) fence_proxy_async_smem();
     __syncthreads();  // tile complete; lam_s / part_s free for the next item
-    if (tid == 0) {
-      if (kTmaOut) {
+    if (tid == 0 && kTmaOut) {
 #pragma unroll
-        for (int hh = 0; hh < kH; ++hh) tma_store_3d(&tmap_o, xs + hh * (kL * 128), hh * kHD, t0, b);
-        bulk_commit();
-      }
-      if (k + 2 * G < p.nitems) {
-        if (kTmaOut) bulk_wait_read0();  // the store has read this tile
-        issue_load(k + 2 * G, buf);
-      }
+      for (int hh = 0; hh < kH; ++hh) tma_store_3d(&tmap_o, xs + hh * (kL * 128), hh * kHD, t0, b);
+      bulk_commit();
     }
+    pend_k = k + 2 * G;  // loaded into this buffer during the next item
   }
 
   if (tid == 0 && kTmaOut) bulk_wait0();
