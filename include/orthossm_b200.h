@@ -100,6 +100,24 @@ size_t ossm_fwd_workspace_bytes(const ossm_fwd_args* a);
 int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_t workspace_bytes,
                        ossm_stream_t stream);
 
+/* ossm_cheby_ema_fwd for callers that cannot allocate device memory (a host
+ * whose allocator owns all device memory, a plugin that is only handed its
+ * input and output buffers).  No counterpart in the reference: its kernels
+ * allocate their scratch through torch.
+ *
+ * The scratch comes from one fixed array of OSSM_NOALLOC_SCRATCH_BYTES inside
+ * the library, held on every GPU that loads the library until the process
+ * exits.  Arguments whose ossm_fwd_workspace_bytes exceeds it are rejected
+ * with OSSM_EWORKSPACE before any launch (16 MiB covers, for example, bf16
+ * x with 8 heads of 64 and B * S up to 65,024 tokens on the fast path).  All
+ * calls on a GPU share the array, so calls that overlap on the GPU race on it.
+ * The first call on each GPU sets the array up (device address, a clear on
+ * `stream`): make it before other work that could overlap it and before any
+ * stream capture.  If `scratch` is not NULL it receives the array's device
+ * address, for ossm_workspace_status. */
+#define OSSM_NOALLOC_SCRATCH_BYTES (16u << 20)
+int ossm_cheby_ema_fwd_noalloc(const ossm_fwd_args* a, ossm_stream_t stream, void** scratch);
+
 /* The per-token decay of the gate alone: lam_tok[b,t,h] (f32, [B,S,H]) from
  * a->x, a->gate_w, a->gate_b, a->lam_h, a->gate_scale/lo/hi.  Feeding the
  * result back through a->lam_tok gives the same output as the gated call.

@@ -17,9 +17,11 @@ OSSM_EVAL_CLENSHAW, OSSM_EVAL_LUT, OSSM_EVAL_CLENSHAW_DEG4 = 0, 1, 2
 OSSM_F_FASTPATH = 1 << 2
 OSSM_F_PRECISE = 1 << 3
 OSSM_F_GENERIC = 1 << 4
+OSSM_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 EXPORTED = (
-    "ossm_fwd_workspace_bytes", "ossm_cheby_ema_fwd", "ossm_gate_decay", "ossm_workspace_status",
+    "ossm_fwd_workspace_bytes", "ossm_cheby_ema_fwd", "ossm_cheby_ema_fwd_noalloc", "ossm_gate_decay",
+    "ossm_workspace_status",
     "ossm_cheby_rkv_lion", "ossm_version", "ossm_status_string",
     "ossm_sizeof_fwd_args", "ossm_sizeof_lion_args",
 )
@@ -63,6 +65,8 @@ def _declare(lib):
     lib.ossm_fwd_workspace_bytes.argtypes = [C.POINTER(FwdArgs)]
     lib.ossm_cheby_ema_fwd.restype = C.c_int
     lib.ossm_cheby_ema_fwd.argtypes = [C.POINTER(FwdArgs), _vp, C.c_size_t, _vp]
+    lib.ossm_cheby_ema_fwd_noalloc.restype = C.c_int
+    lib.ossm_cheby_ema_fwd_noalloc.argtypes = [C.POINTER(FwdArgs), _vp, C.POINTER(_vp)]
     lib.ossm_gate_decay.restype = C.c_int
     lib.ossm_gate_decay.argtypes = [C.POINTER(FwdArgs), _vp, _vp]
     lib.ossm_workspace_status.restype = C.c_int
