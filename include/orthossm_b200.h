@@ -59,6 +59,10 @@ enum ossm_dtype { OSSM_F32 = 0, OSSM_BF16 = 1 };
 /* Use the generic forward kernel even where the TMA / tcgen05 path applies
  * (the two paths compute the same function; used to test one against the other). */
 #define OSSM_F_GENERIC (1u << 4)
+/* On the bf16 fast path (bf16 x, 8 heads of 64), use the single-pass kernel
+ * (chunk look-back across CTAs) instead of the default three-pass one
+ * (chunk aggregates, carry scan, outputs).  Same function; kept for comparison. */
+#define OSSM_F_SINGLE_PASS (1u << 5)
 
 /* ---------------------------------------------------------------------------
  * Fused softsign -> Chebyshev -> gamma_h damping -> tanh -> lambda-EMA scan.
@@ -109,7 +113,7 @@ int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_t workspace
  * the library, held on every GPU that loads the library until the process
  * exits.  Arguments whose ossm_fwd_workspace_bytes exceeds it are rejected
  * with OSSM_EWORKSPACE before any launch (16 MiB covers, for example, bf16
- * x with 8 heads of 64 and B * S up to 65,024 tokens on the fast path).  All
+ * x with 8 heads of 64 and the gate on, up to about 100,000 tokens B * S).  All
  * calls on a GPU share the array, so calls that overlap on the GPU race on it.
  * The first call on each GPU sets the array up (device address, a clear on
  * `stream`): make it before other work that could overlap it and before any

@@ -17,6 +17,7 @@ OSSM_EVAL_CLENSHAW, OSSM_EVAL_LUT, OSSM_EVAL_CLENSHAW_DEG4 = 0, 1, 2
 OSSM_F_FASTPATH = 1 << 2
 OSSM_F_PRECISE = 1 << 3
 OSSM_F_GENERIC = 1 << 4
+OSSM_F_SINGLE_PASS = 1 << 5
 OSSM_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 EXPORTED = (

@@ -411,6 +411,8 @@ using namespace ossm;
 bool ossm_tc_eligible(const ossm_fwd_args* a);
 size_t ossm_tc_workspace_bytes(const ossm_fwd_args* a);
 int ossm_tc_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
+size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a);
+int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
 
 namespace {
 
@@ -477,7 +479,8 @@ FwdLayout fwd_layout(const ossm_fwd_args* a) {
   l.off_lam = off;
   if (a->gate_w && !a->lam_tok) off = align256(off + (size_t)a->B * a->S * a->H * 4);
   l.total = off;
-  if (ossm_tc_eligible(a)) l.total = ossm_tc_workspace_bytes(a);  // fast path records
+  if (ossm_tc_eligible(a))  // bf16 fast paths: whichever layout the flags select
+    l.total = (a->flags & OSSM_F_SINGLE_PASS) ? ossm_tc_workspace_bytes(a) : ossm_p3_workspace_bytes(a);
   return l;
 }
 
@@ -570,7 +573,8 @@ extern "C" int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_
   p.incB = reinterpret_cast<float*>(ws + l.off_incB);
   p.nctas = (uint32_t)l.N;
 
-  if (ossm_tc_eligible(a)) return ossm_tc_launch(a, ws, st);
+  if (ossm_tc_eligible(a))
+    return (a->flags & OSSM_F_SINGLE_PASS) ? ossm_tc_launch(a, ws, st) : ossm_p3_launch(a, ws, st);
 
   if (a->gate_w && !a->lam_tok) {
     if (launch_gate(a, reinterpret_cast<float*>(ws + l.off_lam), st) != cudaSuccess) return OSSM_ELAUNCH;

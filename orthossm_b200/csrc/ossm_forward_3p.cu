@@ -1,0 +1,498 @@
+// Three-pass forward for bf16 activations, 8 heads x head_dim 64 (sm_100a).
+//
+// Same arithmetic contract as fwd_scan_kernel in ossm_forward.cu (which
+// restates _fused_clenshaw_ema_kernel, sdpc_kernel.py:988-1209).  The EMA
+// s_t = a_t s_{t-1} + (1 - a_t) u_t is a first-order linear recurrence, so the
+// sequence is split into 32-token chunks and solved in three launches, none of
+// which waits on another CTA:
+//
+//   p3_agg_kernel    one CTA per (b, chunk), warp = head: TMA-loads the
+//                    [32 x 512] tile, forms the decays (the optional gate as a
+//                    [32 x 512] . [512 x 8] tensor-core product with the weights
+//                    held in registers), evaluates u and runs the EMA from a zero
+//                    state.  Writes the chunk's end state and decay product (and
+//                    the per-token decays when gated).
+//   p3_carry_kernel  one CTA per (b, h) chain: the carry into every chunk,
+//                    c_k = A_{k-1} c_{k-1} + agg_{k-1}, in a fixed order
+//                    (16 spans folded in parallel, then across spans).
+//   p3_out_kernel    one CTA per (b, chunk), warp = head: re-reads x, evaluates
+//                    u again and runs the EMA from the chunk's carry, writing
+//                    each output as it is produced.
+//
+// Every launch streams with high occupancy and no inter-CTA waits; the price is
+// a second evaluation and a second read of x.  Results are bitwise
+// reproducible (every fold has a fixed order).
+//
+// NaN and infinite inputs are handled off the hot path: the fast evaluation
+// lets them surface as NaN, each warp checks its chunk once and recomputes it
+// with the reference's semantics.
+#include <cudaTypedefs.h>
+
+#include "ossm_sm100.cuh"
+
+// shared with the single-pass path (ossm_forward_tc.cu)
+namespace ossm {
+namespace fast {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
+bool encode_map(CUtensorMap* map, const void* base, int S, int B, long long ss, long long sb);
+}  // namespace fast
+}  // namespace ossm
+
+namespace ossm {
+namespace p3 {
+
+constexpr int kNT = 256;
+constexpr int kH = 8;    // heads (one warp each)
+constexpr int kHD = 64;  // channels per head
+constexpr int kD = kH * kHD;
+constexpr int kL = 32;               // tokens per chunk
+constexpr int kBox = kL * 128;       // one head's [32 x 128 B] box
+constexpr int kTile = kH * kBox;     // 32 KB
+constexpr int kOffPart = kTile;                       // [8 warps][32 tokens][8] f32
+constexpr int kOffLam = kOffPart + kH * kL * kH * 4;  // [8 heads][32] float4
+constexpr int kOffBar = kOffLam + kH * kL * 16;
+constexpr int kAggSmem = kOffBar + 16 + 1024;        // + alignment slack
+constexpr int kSpans = 16;                           // carry kernel: warps per chain
+
+struct Params {
+  int B, S, K, nchunks;
+  const __nv_bfloat16* x;
+  long long xsb, xss;
+  const float* coeffs;
+  const float* lam_h;
+  float momentum;
+  const float* gate_w;
+  const float* gate_b;
+  float gate_scale, gate_lo, gate_hi;
+  const float* lam_in;  // caller's per-token decay [B,S,H] or NULL
+  float* lam_ws;        // per-token decays written by the gate [B,S,H] (workspace)
+  const float* init;
+  float* fin;
+  void* out;
+  long long osb, oss;
+  float* A;      // [N] chunk decay products
+  float* agg;    // [N][64] chunk end states from zero (chunk 0: from the carried-in state)
+  float* carry;  // [N][64] state entering each chunk
+  WsHeader* ws;  // sticky status (a tile that never arrived)
+};
+
+OSSM_DEV float clamp4_nan(float v) {  // NaN-propagating clamp to [-4, 4]
+  float r;
+  asm("max.NaN.f32 %0, %1, 0fC0800000;\n\tmin.NaN.f32 %0, %0, 0f40800000;" : "=f"(r) : "f"(v));
+  return r;
+}
+OSSM_DEV float rcp_approx(float x) {  // keeps subnormal results: huge |x| still gives x * rcp(1 + |x|) ~ 1
+  float y;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Chebyshev -> monomial coefficients with gamma folded in (T_0..T_7 written out).
+OSSM_DEV void cheb_to_mono(const float2 (&ck)[8], float gamma, float2 (&a)[8]) {
+  const float2 g2 = make_float2(gamma, gamma);
+  auto w = [](float v) { return make_float2(v, v); };
+  a[0] = mul2(fma2(w(-1.f), ck[6], fma2(w(1.f), ck[4], fma2(w(-1.f), ck[2], ck[0]))), g2);
+  a[1] = mul2(fma2(w(-7.f), ck[7], fma2(w(5.f), ck[5], fma2(w(-3.f), ck[3], ck[1]))), g2);
+  a[2] = mul2(fma2(w(18.f), ck[6], fma2(w(-8.f), ck[4], mul2(w(2.f), ck[2]))), g2);
+  a[3] = mul2(fma2(w(56.f), ck[7], fma2(w(-20.f), ck[5], mul2(w(4.f), ck[3]))), g2);
+  a[4] = mul2(fma2(w(-48.f), ck[6], mul2(w(8.f), ck[4])), g2);
+  a[5] = mul2(fma2(w(-112.f), ck[7], mul2(w(16.f), ck[5])), g2);
+  a[6] = mul2(mul2(w(32.f), ck[6]), g2);
+  a[7] = mul2(mul2(w(64.f), ck[7]), g2);
+}
+
+// The lane's coefficients of (b, h): raw (precise) or gamma-folded monomial.
+template <bool PRECISE>
+OSSM_DEV void load_coeffs(const Params& p, int b, int h, int j0, float gamma, float2 (&cf)[8]) {
+  const float* cb = p.coeffs + ((size_t)(b * kH + h) * p.K) * kHD + j0;
+  float2 ck[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    ck[q] = q < p.K ? __ldg(reinterpret_cast<const float2*>(cb + q * kHD)) : make_float2(0.f, 0.f);
+  if (PRECISE) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) cf[q] = ck[q];
+  } else {
+    cheb_to_mono(ck, gamma, cf);
+  }
+}
+
+// u = tanh(clamp(gamma y(xn), +-4)) for the lane's 2 channels of one token.
+// EXACT: the reference's semantics for every input (NaN -> u = 0,
+// sdpc_kernel.py:1164; +-inf -> xn = +-1, :1078-1085).  Otherwise NaN and
+// +-inf inputs come out as NaN (caught per chunk); every finite input takes the
+// reference's formula either way.
+template <bool PRECISE, bool EXACT>
+OSSM_DEV float2 eval_u(uint32_t raw, const float2 (&cf)[8], float gamma) {
+  const float x0 = __uint_as_float(raw << 16), x1 = __uint_as_float(raw & 0xffff0000u);
+  float2 xn;
+  if (PRECISE || EXACT) {
+    float xa, sg;
+    xn.x = softsign<PRECISE>(x0, false, xa, sg);
+    xn.y = softsign<PRECISE>(x1, false, xa, sg);
+    if (!EXACT) {
+      if (x0 != x0) xn.x = x0;
+      if (x1 != x1) xn.y = x1;
+    }
+  } else {  // x / (1 + |x|); inf / inf = NaN
+    xn = make_float2(x0 * rcp_approx(1.0f + fabsf(x0)), x1 * rcp_approx(1.0f + fabsf(x1)));
+  }
+  float2 y;
+  if (PRECISE) {  // Clenshaw on the raw coefficients, then gamma
+    const float2 x2 = make_float2(2.f * xn.x, 2.f * xn.y);
+    float2 u1 = cf[7], u2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int q = 6; q >= 1; --q) {
+      const float2 tt = fma2(x2, u1, sub2(cf[q], u2));
+      u2 = u1;
+      u1 = tt;
+    }
+    y = fma2(xn, u1, sub2(cf[0], u2));
+    y = make_float2(y.x * gamma, y.y * gamma);
+  } else {  // Horner on gamma-folded monomial coefficients
+    y = cf[7];
+#pragma unroll
+    for (int q = 6; q >= 0; --q) y = fma2(y, xn, cf[q]);
+  }
+  if (EXACT) {
+    const float z0 = fminf(fmaxf(y.x, -4.f), 4.f), z1 = fminf(fmaxf(y.y, -4.f), 4.f);
+    return make_float2(x0 != x0 ? 0.f : (PRECISE ? tanhf(z0) : tanh_fast(z0)),
+                       x1 != x1 ? 0.f : (PRECISE ? tanhf(z1) : tanh_fast(z1)));
+  }
+  const float z0 = clamp4_nan(y.x), z1 = clamp4_nan(y.y);
+  return make_float2(PRECISE ? tanhf(z0) : tanh_fast(z0), PRECISE ? tanhf(z1) : tanh_fast(z1));
+}
+
+// s <- l s + (1 - l) u; token 0 of the sequence (first) folds the carried-in
+// state with the reference's clamp.
+OSSM_DEV float2 ema_step(float2 s, float4 lm, float2 u, bool first) {
+  if (first) return make_float2(clamp1(fmaf(lm.x, s.x, lm.z * u.x)), clamp1(fmaf(lm.y, s.y, lm.w * u.y)));
+  return fma2(make_float2(lm.x, lm.y), s, mul2(make_float2(lm.z, lm.w), u));
+}
+
+// The 32-token EMA of one chunk from state s (decays lam[0..31]); RAW(t) gives
+// the packed bf16 pair of token t, OUT(t, s) receives each state.
+template <bool PRECISE, bool EXACT, typename RawF, typename OutF>
+OSSM_DEV float2 ema_chunk(float2 s, const float4* lam, bool first, const float2 (&cf)[8], float gamma, RawF raw,
+                          OutF out) {
+#pragma unroll
+  for (int t = 0; t < kL; ++t) {
+    s = ema_step(s, lam[t], eval_u<PRECISE, EXACT>(raw(t), cf, gamma), t == 0 && first);
+    out(t, s);
+  }
+  return s;
+}
+// The same with the reference's NaN / inf semantics as a rolled loop (the rare
+// recompute of a chunk that held such inputs).
+template <bool PRECISE, typename RawF, typename OutF>
+OSSM_DEV float2 ema_chunk_exact(float2 s, const float4* lam, bool first, const float2 (&cf)[8], float gamma,
+                                RawF raw, OutF out) {
+#pragma unroll 1
+  for (int t = 0; t < kL; ++t) {
+    s = ema_step(s, lam[t], eval_u<PRECISE, true>(raw(t), cf, gamma), t == 0 && first);
+    out(t, s);
+  }
+  return s;
+}
+
+OSSM_DEV void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+OSSM_DEV void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// byte offset of (token t, 16-byte chunk j) in a head's 128-byte-swizzled box
+OSSM_DEV uint32_t box_off(int t, int j) { return (uint32_t)(t * 128 + ((j ^ (t & 7)) << 4)); }
+
+// Decay of token (t0 + lane), head h, from a per-token input or the constant.
+OSSM_DEV float lam_token(const Params& p, const float* lam_tok, int b, int tg, int h, float lam_base) {
+  if (tg >= p.S) return 1.f;  // past the end: the state is carried unchanged
+  return lam_tok ? __ldg(lam_tok + ((size_t)b * p.S + tg) * kH + h) : lam_base;
+}
+
+// ---------------------------------------------------------------------------
+// pass 1: chunk aggregates
+// ---------------------------------------------------------------------------
+template <bool GATE, bool PRECISE>
+__global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
+  using namespace sm100;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* part_s = reinterpret_cast<float*>(sm + kOffPart);
+  float4* lam_s = reinterpret_cast<float4*>(sm + kOffLam);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
+  const int j0 = lane * 2;
+  const int c = (int)(blockIdx.x / p.B), b = (int)(blockIdx.x % p.B);
+  const int t0 = c * kL, tg = t0 + lane;
+  const float gamma = 0.98f - 0.06f * (float)h / (float)kH;
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(bar, kTile);
+#pragma unroll
+    for (int hh = 0; hh < kH; ++hh) tma_load_3d(sm + hh * kBox, &tmap_x, bar, hh * kHD, t0, b);
+  }
+  // while the tile lands: coefficients, gate weights, the caller's decay
+  float2 cf[8];
+  load_coeffs<PRECISE>(p, b, h, j0, gamma, cf);
+  const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
+  float lam = GATE ? lam_base : lam_token(p, p.lam_in, b, tg, h, lam_base);
+  uint32_t whi[4][2], wlo[4][2];  // mma B fragments of W[gid][h*64 + ks*16 + ...], split bf16 hi + lo
+  float bias_h = 0.f;
+  if (GATE) {
+    const int gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const float* wr = p.gate_w + (size_t)gid * kD + h * kHD + ks * 16 + 2 * tig;
+      const float2 w01 = __ldg(reinterpret_cast<const float2*>(wr));
+      const float2 w89 = __ldg(reinterpret_cast<const float2*>(wr + 8));
+      const float hw[4] = {w01.x, w01.y, w89.x, w89.y};
+      __nv_bfloat16 hi[4], lo[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        hi[q] = __float2bfloat16_rn(hw[q]);
+        lo[q] = __float2bfloat16_rn(hw[q] - __bfloat162float(hi[q]));
+      }
+      whi[ks][0] = pack_bf16x2(__bfloat162float(hi[0]), __bfloat162float(hi[1]));
+      whi[ks][1] = pack_bf16x2(__bfloat162float(hi[2]), __bfloat162float(hi[3]));
+      wlo[ks][0] = pack_bf16x2(__bfloat162float(lo[0]), __bfloat162float(lo[1]));
+      wlo[ks][1] = pack_bf16x2(__bfloat162float(lo[2]), __bfloat162float(lo[3]));
+    }
+    bias_h = __ldg(p.gate_b + h);
+  }
+  __syncthreads();  // the mbarrier is initialised
+  const bool ok = mbar_wait(bar, 0);
+  const uint8_t* xs = sm + h * kBox;
+
+  if (GATE) {  // this head's 64-channel partial logits for all 8 heads, then the sum
+    const uint32_t xa = smem_u32(xs);
+    const int m = lane >> 3, rr = lane & 7, gid = lane >> 2, tig = lane & 3;
+    float* pw = part_s + h * (kL * kH);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t a[4];
+        // A: tokens mt*16 + (m&1)*8 + rr, channels ks*16 + (m>>1)*8 of this head
+        ldmatrix_x4(xa + box_off(mt * 16 + (m & 1) * 8 + rr, ks * 2 + (m >> 1)), a);
+        mma_bf16_16816(d, a, whi[ks][0], whi[ks][1]);
+        mma_bf16_16816(d, a, wlo[ks][0], wlo[ks][1]);
+      }
+      pw[(mt * 16 + gid) * kH + 2 * tig] = d[0];
+      pw[(mt * 16 + gid) * kH + 2 * tig + 1] = d[1];
+      pw[(mt * 16 + gid + 8) * kH + 2 * tig] = d[2];
+      pw[(mt * 16 + gid + 8) * kH + 2 * tig + 1] = d[3];
+    }
+    __syncthreads();
+    float logit = bias_h;
+#pragma unroll
+    for (int g = 0; g < kH; ++g) logit += part_s[g * (kL * kH) + lane * kH + h];
+    const float sg = 1.0f / (1.0f + __expf(-logit));
+    lam = fminf(fmaxf(lam_base + p.gate_scale * (sg - 0.5f), p.gate_lo), p.gate_hi);
+    if (tg < p.S) p.lam_ws[((size_t)b * p.S + tg) * kH + h] = lam;  // for the output pass
+    else lam = 1.f;
+  }
+  float a = tg == 0 ? 0.f : lam;  // the chunk's decay product (the carry enters at token 0)
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) a *= __shfl_xor_sync(0xffffffffu, a, o);
+  lam_s[h * kL + lane] = make_float4(lam, lam, 1.f - lam, 1.f - lam);
+  __syncwarp();
+
+  float2 s = make_float2(0.f, 0.f);
+  if (c == 0 && p.init) s = __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + h * kHD + j0));
+  const float2 s_in = s;
+  auto raw = [&](int t) { return *reinterpret_cast<const uint32_t*>(xs + box_off(t, lane >> 2) + (lane & 3) * 4); };
+  auto none = [](int, float2) {};
+  s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, c == 0, cf, gamma, raw, none);
+  if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y))  // NaN / inf inputs: the reference's semantics
+    s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, c == 0, cf, gamma, raw, none);
+  const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
+  *reinterpret_cast<float2*>(p.agg + n * kHD + j0) = s;
+  if (lane == 0) p.A[n] = a;
+  if (!ok && lane == 0) atomicExch(&p.ws->status, (uint32_t)OSSM_ETIMEOUT);
+}
+
+// ---------------------------------------------------------------------------
+// pass 2: carries (one CTA per (b, h) chain; warp w folds span w, lane = 2 channels)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kSpans * 32) p3_carry_kernel(const Params p) {
+  __shared__ float2 spanB[kSpans][32];
+  __shared__ float spanA[kSpans];
+  __shared__ float2 spanX[kSpans][32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t n0 = (size_t)blockIdx.x * p.nchunks;
+  const int per = (p.nchunks + kSpans - 1) / kSpans;
+  const int c0 = min(w * per, p.nchunks), c1 = min(c0 + per, p.nchunks);
+  // span aggregate: state after the span from zero, and its decay product
+  float2 B = make_float2(0.f, 0.f);
+  float A = 1.f;
+  for (int c = c0; c < c1; ++c) {
+    const float Ac = __ldg(p.A + n0 + c);
+    const float2 g = __ldg(reinterpret_cast<const float2*>(p.agg + (n0 + c) * kHD) + lane);
+    B = fma2(make_float2(Ac, Ac), B, g);
+    A *= Ac;
+  }
+  spanB[w][lane] = B;
+  if (lane == 0) spanA[w] = A;
+  __syncthreads();
+  if (w == 0) {  // carries into the spans, in span order
+    float2 X = make_float2(0.f, 0.f);
+    for (int q = 0; q < kSpans; ++q) {
+      spanX[q][lane] = X;
+      X = fma2(make_float2(spanA[q], spanA[q]), X, spanB[q][lane]);
+    }
+  }
+  __syncthreads();
+  float2 X = spanX[w][lane];
+  for (int c = c0; c < c1; ++c) {
+    reinterpret_cast<float2*>(p.carry + (n0 + c) * kHD)[lane] = X;
+    const float Ac = __ldg(p.A + n0 + c);
+    const float2 g = __ldg(reinterpret_cast<const float2*>(p.agg + (n0 + c) * kHD) + lane);
+    X = fma2(make_float2(Ac, Ac), X, g);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// pass 3: outputs from the carries
+// ---------------------------------------------------------------------------
+template <bool PRECISE, typename OT>
+__global__ void __launch_bounds__(kNT) p3_out_kernel(const Params p, const float* lam_tok) {
+  __shared__ float4 lam_s[kH * kL];
+  const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
+  const int j0 = lane * 2, ch0 = h * kHD + j0;
+  const int c = (int)(blockIdx.x / p.B), b = (int)(blockIdx.x % p.B);
+  const int t0 = c * kL, nt = min(kL, p.S - t0);
+  const float gamma = 0.98f - 0.06f * (float)h / (float)kH;
+  const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
+
+  // x of this chunk (L2 or HBM), the carry, the decays, the coefficients
+  const __nv_bfloat16* xp = p.x + (size_t)b * p.xsb + (size_t)t0 * p.xss + ch0;
+  uint32_t r[kL];
+#pragma unroll
+  for (int t = 0; t < kL; ++t)
+    r[t] = t < nt ? __ldcs(reinterpret_cast<const unsigned int*>(xp + (size_t)t * p.xss)) : 0u;
+  float2 X;
+  if (c == 0)
+    X = p.init ? __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + ch0)) : make_float2(0.f, 0.f);
+  else
+    X = *reinterpret_cast<const float2*>(p.carry + n * kHD + j0);
+  const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
+  const float lam = lam_token(p, lam_tok, b, t0 + lane, h, lam_base);
+  lam_s[h * kL + lane] = make_float4(lam, lam, 1.f - lam, 1.f - lam);
+  float2 cf[8];
+  load_coeffs<PRECISE>(p, b, h, j0, gamma, cf);
+  __syncwarp();
+
+  OT* op = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + (size_t)t0 * p.oss + ch0;
+  auto raw = [&](int t) { return r[t]; };
+  auto emit = [&](int t, float2 v) {
+    if (t < nt) st2(op + (size_t)t * p.oss, sizeof(OT) == 4 ? make_float2(clamp1(v.x), clamp1(v.y)) : v);
+  };
+  float2 s = ema_chunk<PRECISE, false>(X, lam_s + h * kL, c == 0, cf, gamma, raw, emit);
+  if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y)) {  // NaN / inf inputs: redo with the reference's semantics
+    auto reraw = [&](int t) {
+      return t < nt ? __ldcs(reinterpret_cast<const unsigned int*>(xp + (size_t)t * p.xss)) : 0u;
+    };
+    s = ema_chunk_exact<PRECISE>(X, lam_s + h * kL, c == 0, cf, gamma, reraw, emit);
+  }
+  // decays are 1 past the end, so the chunk's last state is the sequence's final state
+  if (p.fin && t0 + kL >= p.S)
+    *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) = make_float2(clamp1(s.x), clamp1(s.y));
+}
+
+template <bool GATE, bool PRECISE>
+cudaError_t launch_agg(const CUtensorMap& mx, const Params& p, cudaStream_t st) {
+  auto kern = p3_agg_kernel<GATE, PRECISE>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAggSmem);
+  if (e != cudaSuccess) return e;
+  kern<<<p.B * p.nchunks, kNT, kAggSmem, st>>>(mx, p);
+  return cudaGetLastError();
+}
+
+template <bool PRECISE, typename OT>
+cudaError_t launch_out(const Params& p, const float* lam_tok, cudaStream_t st) {
+  p3_out_kernel<PRECISE, OT><<<p.B * p.nchunks, kNT, 0, st>>>(p, lam_tok);
+  return cudaGetLastError();
+}
+
+}  // namespace p3
+}  // namespace ossm
+
+using namespace ossm;
+
+// Workspace of the three-pass path: header, decay products, aggregates,
+// carries and (gated) the per-token decays.
+size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a) {
+  const size_t nch = (size_t)(a->S + p3::kL - 1) / p3::kL;
+  const size_t N = (size_t)a->B * p3::kH * nch;
+  auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+  size_t bytes = al(sizeof(WsHeader)) + al(N * 4) + 2 * al(N * p3::kHD * 4);
+  if (a->gate_w && !a->lam_tok) bytes += al((size_t)a->B * a->S * p3::kH * 4);
+  return bytes;
+}
+
+int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
+  using namespace p3;
+  Params p;
+  p.B = a->B;
+  p.S = a->S;
+  p.K = (a->flags & OSSM_EVAL_MASK) == OSSM_EVAL_CLENSHAW_DEG4 ? (a->degree < 4 ? a->degree : 4) : a->degree;
+  p.nchunks = (a->S + kL - 1) / kL;
+  p.x = reinterpret_cast<const __nv_bfloat16*>(a->x);
+  p.xsb = a->x_stride_b;
+  p.xss = a->x_stride_s;
+  p.coeffs = a->coeffs;
+  p.lam_h = a->lam_h;
+  p.momentum = a->momentum;
+  const bool gate = a->gate_w && !a->lam_tok;
+  p.gate_w = a->gate_w;
+  p.gate_b = a->gate_b;
+  p.gate_scale = a->gate_scale;
+  p.gate_lo = a->gate_lo;
+  p.gate_hi = a->gate_hi;
+  p.lam_in = a->lam_tok;
+  p.init = a->init_state;
+  p.fin = a->final_state;
+  p.out = a->out;
+  p.osb = a->out_stride_b;
+  p.oss = a->out_stride_s;
+  const size_t N = (size_t)a->B * kH * p.nchunks;
+  auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+  p.ws = reinterpret_cast<WsHeader*>(ws);
+  size_t off = al(sizeof(WsHeader));
+  p.A = reinterpret_cast<float*>(ws + off);
+  off += al(N * 4);
+  p.agg = reinterpret_cast<float*>(ws + off);
+  off += al(N * kHD * 4);
+  p.carry = reinterpret_cast<float*>(ws + off);
+  off += al(N * kHD * 4);
+  p.lam_ws = gate ? reinterpret_cast<float*>(ws + off) : nullptr;
+  if ((long long)a->B * p.nchunks > 0x7fffffffLL) return OSSM_EINVAL;
+
+  CUtensorMap mx;
+  if (!fast::encode_map(&mx, a->x, a->S, a->B, a->x_stride_s, a->x_stride_b)) return OSSM_EINVAL;
+  const bool precise = (a->out_dtype == OSSM_F32) || (a->flags & OSSM_F_PRECISE);
+  cudaError_t e;
+  if (precise)
+    e = gate ? launch_agg<true, true>(mx, p, st) : launch_agg<false, true>(mx, p, st);
+  else
+    e = gate ? launch_agg<true, false>(mx, p, st) : launch_agg<false, false>(mx, p, st);
+  if (e != cudaSuccess) return OSSM_ELAUNCH;
+  p3_carry_kernel<<<a->B * kH, kSpans * 32, 0, st>>>(p);
+  if ((e = cudaGetLastError()) != cudaSuccess) return OSSM_ELAUNCH;
+  const float* lam_tok = gate ? p.lam_ws : a->lam_tok;
+  if (a->out_dtype == OSSM_F32)
+    e = launch_out<true, float>(p, lam_tok, st);
+  else
+    e = precise ? launch_out<true, __nv_bfloat16>(p, lam_tok, st) : launch_out<false, __nv_bfloat16>(p, lam_tok, st);
+  return e == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
+}
