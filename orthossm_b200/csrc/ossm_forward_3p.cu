@@ -49,8 +49,8 @@ constexpr int kL = 32;               // tokens per chunk
 constexpr int kBox = kL * 128;       // one head's [32 x 128 B] box
 constexpr int kTile = kH * kBox;     // 32 KB
 constexpr int kOffPart = kTile;                       // [8 warps][32 tokens][8] f32
-constexpr int kOffLam = kOffPart + kH * kL * kH * 4;  // [8 heads][32] float4
-constexpr int kOffBar = kOffLam + kH * kL * 16;
+constexpr int kOffLam = kOffPart + kH * kL * kH * 4;  // [8 heads][32] float2 (l, 1 - l)
+constexpr int kOffBar = kOffLam + kH * kL * 8;
 constexpr int kAggSmem = kOffBar + 16 + 1024;        // + alignment slack
 constexpr int kSpans = 16;                           // carry kernel: warps per chain
 
@@ -103,9 +103,9 @@ OSSM_DEV void cheb_to_mono(const float2 (&ck)[8], float gamma, float2 (&a)[8]) {
 
 // The lane's coefficients of (b, h): raw (precise) or gamma-folded monomial.
 template <bool PRECISE>
-OSSM_DEV void load_coeffs(const Params& p, int b, int h, int j0, float gamma, float2 (&cf)[8]) {
+OSSM_DEV void load_coeffs(const Params& p, int b, int h, int j0, float gamma, float (&c0)[8], float (&c1)[8]) {
   const float* cb = p.coeffs + ((size_t)(b * kH + h) * p.K) * kHD + j0;
-  float2 ck[8];
+  float2 ck[8], cf[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q)
     ck[q] = q < p.K ? __ldg(reinterpret_cast<const float2*>(cb + q * kHD)) : make_float2(0.f, 0.f);
@@ -115,6 +115,8 @@ OSSM_DEV void load_coeffs(const Params& p, int b, int h, int j0, float gamma, fl
   } else {
     cheb_to_mono(ck, gamma, cf);
   }
+#pragma unroll
+  for (int q = 0; q < 8; ++q) c0[q] = cf[q].x, c1[q] = cf[q].y;
 }
 
 // u = tanh(clamp(gamma y(xn), +-4)) for the lane's 2 channels of one token.
@@ -123,61 +125,59 @@ OSSM_DEV void load_coeffs(const Params& p, int b, int h, int j0, float gamma, fl
 // +-inf inputs come out as NaN (caught per chunk); every finite input takes the
 // reference's formula either way.
 template <bool PRECISE, bool EXACT>
-OSSM_DEV float2 eval_u(uint32_t raw, const float2 (&cf)[8], float gamma) {
-  const float x0 = __uint_as_float(raw << 16), x1 = __uint_as_float(raw & 0xffff0000u);
-  float2 xn;
+OSSM_DEV float eval_u1(float x, const float (&c)[8], float gamma) {
+  float xn;
   if (PRECISE || EXACT) {
     float xa, sg;
-    xn.x = softsign<PRECISE>(x0, false, xa, sg);
-    xn.y = softsign<PRECISE>(x1, false, xa, sg);
-    if (!EXACT) {
-      if (x0 != x0) xn.x = x0;
-      if (x1 != x1) xn.y = x1;
-    }
+    xn = softsign<PRECISE>(x, false, xa, sg);
+    if (!EXACT && x != x) xn = x;
   } else {  // x / (1 + |x|); inf / inf = NaN
-    xn = make_float2(x0 * rcp_approx(1.0f + fabsf(x0)), x1 * rcp_approx(1.0f + fabsf(x1)));
+    xn = x * rcp_approx(1.0f + fabsf(x));
   }
-  float2 y;
+  float y;
   if (PRECISE) {  // Clenshaw on the raw coefficients, then gamma
-    const float2 x2 = make_float2(2.f * xn.x, 2.f * xn.y);
-    float2 u1 = cf[7], u2 = make_float2(0.f, 0.f);
+    const float x2 = 2.f * xn;
+    float u1 = c[7], u2 = 0.f;
 #pragma unroll
     for (int q = 6; q >= 1; --q) {
-      const float2 tt = fma2(x2, u1, sub2(cf[q], u2));
+      const float tt = fmaf(x2, u1, c[q] - u2);
       u2 = u1;
       u1 = tt;
     }
-    y = fma2(xn, u1, sub2(cf[0], u2));
-    y = make_float2(y.x * gamma, y.y * gamma);
+    y = fmaf(xn, u1, c[0] - u2) * gamma;
   } else {  // Horner on gamma-folded monomial coefficients
-    y = cf[7];
+    y = c[7];
 #pragma unroll
-    for (int q = 6; q >= 0; --q) y = fma2(y, xn, cf[q]);
+    for (int q = 6; q >= 0; --q) y = fmaf(y, xn, c[q]);
   }
   if (EXACT) {
-    const float z0 = fminf(fmaxf(y.x, -4.f), 4.f), z1 = fminf(fmaxf(y.y, -4.f), 4.f);
-    return make_float2(x0 != x0 ? 0.f : (PRECISE ? tanhf(z0) : tanh_fast(z0)),
-                       x1 != x1 ? 0.f : (PRECISE ? tanhf(z1) : tanh_fast(z1)));
+    const float z = fminf(fmaxf(y, -4.f), 4.f);
+    return x != x ? 0.f : (PRECISE ? tanhf(z) : tanh_fast(z));
   }
-  const float z0 = clamp4_nan(y.x), z1 = clamp4_nan(y.y);
-  return make_float2(PRECISE ? tanhf(z0) : tanh_fast(z0), PRECISE ? tanhf(z1) : tanh_fast(z1));
+  const float z = clamp4_nan(y);
+  return PRECISE ? tanhf(z) : tanh_fast(z);
+}
+template <bool PRECISE, bool EXACT>
+OSSM_DEV float2 eval_u(uint32_t raw, const float (&c0)[8], const float (&c1)[8], float gamma) {
+  return make_float2(eval_u1<PRECISE, EXACT>(__uint_as_float(raw << 16), c0, gamma),
+                     eval_u1<PRECISE, EXACT>(__uint_as_float(raw & 0xffff0000u), c1, gamma));
 }
 
 // s <- l s + (1 - l) u; token 0 of the sequence (first) folds the carried-in
 // state with the reference's clamp.
-OSSM_DEV float2 ema_step(float2 s, float4 lm, float2 u, bool first) {
-  if (first) return make_float2(clamp1(fmaf(lm.x, s.x, lm.z * u.x)), clamp1(fmaf(lm.y, s.y, lm.w * u.y)));
-  return fma2(make_float2(lm.x, lm.y), s, mul2(make_float2(lm.z, lm.w), u));
+OSSM_DEV float2 ema_step(float2 s, float2 lm, float2 u, bool first) {  // lm = (l, 1 - l)
+  const float2 r = make_float2(fmaf(lm.x, s.x, lm.y * u.x), fmaf(lm.x, s.y, lm.y * u.y));
+  return first ? make_float2(clamp1(r.x), clamp1(r.y)) : r;
 }
 
 // The 32-token EMA of one chunk from state s (decays lam[0..31]); RAW(t) gives
 // the packed bf16 pair of token t, OUT(t, s) receives each state.
 template <bool PRECISE, bool EXACT, typename RawF, typename OutF>
-OSSM_DEV float2 ema_chunk(float2 s, const float4* lam, bool first, const float2 (&cf)[8], float gamma, RawF raw,
-                          OutF out) {
+OSSM_DEV float2 ema_chunk(float2 s, const float2* lam, bool first, const float (&c0)[8], const float (&c1)[8],
+                          float gamma, RawF raw, OutF out) {
 #pragma unroll
   for (int t = 0; t < kL; ++t) {
-    s = ema_step(s, lam[t], eval_u<PRECISE, EXACT>(raw(t), cf, gamma), t == 0 && first);
+    s = ema_step(s, lam[t], eval_u<PRECISE, EXACT>(raw(t), c0, c1, gamma), t == 0 && first);
     out(t, s);
   }
   return s;
@@ -185,11 +185,11 @@ OSSM_DEV float2 ema_chunk(float2 s, const float4* lam, bool first, const float2 
 // The same with the reference's NaN / inf semantics as a rolled loop (the rare
 // recompute of a chunk that held such inputs).
 template <bool PRECISE, typename RawF, typename OutF>
-OSSM_DEV float2 ema_chunk_exact(float2 s, const float4* lam, bool first, const float2 (&cf)[8], float gamma,
-                                RawF raw, OutF out) {
+OSSM_DEV float2 ema_chunk_exact(float2 s, const float2* lam, bool first, const float (&c0)[8], const float (&c1)[8],
+                                float gamma, RawF raw, OutF out) {
 #pragma unroll 1
   for (int t = 0; t < kL; ++t) {
-    s = ema_step(s, lam[t], eval_u<PRECISE, true>(raw(t), cf, gamma), t == 0 && first);
+    s = ema_step(s, lam[t], eval_u<PRECISE, true>(raw(t), c0, c1, gamma), t == 0 && first);
     out(t, s);
   }
   return s;
@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* part_s = reinterpret_cast<float*>(sm + kOffPart);
-  float4* lam_s = reinterpret_cast<float4*>(sm + kOffLam);
+  float2* lam_s = reinterpret_cast<float2*>(sm + kOffLam);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
   const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
   const int j0 = lane * 2;
@@ -241,8 +241,8 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
     for (int hh = 0; hh < kH; ++hh) tma_load_3d(sm + hh * kBox, &tmap_x, bar, hh * kHD, t0, b);
   }
   // while the tile lands: coefficients, gate weights, the caller's decay
-  float2 cf[8];
-  load_coeffs<PRECISE>(p, b, h, j0, gamma, cf);
+  float c0[8], c1[8];
+  load_coeffs<PRECISE>(p, b, h, j0, gamma, c0, c1);
   const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
   float lam = GATE ? lam_base : lam_token(p, p.lam_in, b, tg, h, lam_base);
   uint32_t whi[4][2], wlo[4][2];  // mma B fragments of W[gid][h*64 + ks*16 + ...], split bf16 hi + lo
@@ -304,17 +304,25 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
   float a = tg == 0 ? 0.f : lam;  // the chunk's decay product (the carry enters at token 0)
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) a *= __shfl_xor_sync(0xffffffffu, a, o);
-  lam_s[h * kL + lane] = make_float4(lam, lam, 1.f - lam, 1.f - lam);
+  lam_s[h * kL + lane] = make_float2(lam, 1.f - lam);
   __syncwarp();
 
   float2 s = make_float2(0.f, 0.f);
   if (c == 0 && p.init) s = __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + h * kHD + j0));
   const float2 s_in = s;
-  auto raw = [&](int t) { return *reinterpret_cast<const uint32_t*>(xs + box_off(t, lane >> 2) + (lane & 3) * 4); };
+  // the lane's 4 bytes of token t sit at t*128 + ((lane/4 ^ t%8) * 16) + (lane%4)*4: 8 row patterns
+  uint32_t roff[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) roff[k] = (uint32_t)((((lane >> 2) ^ k) << 4) + (lane & 3) * 4);
+  auto raw = [&](int t) { return *reinterpret_cast<const uint32_t*>(xs + roff[t & 7] + t * 128); };
   auto none = [](int, float2) {};
-  s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, c == 0, cf, gamma, raw, none);
-  if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y))  // NaN / inf inputs: the reference's semantics
-    s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, c == 0, cf, gamma, raw, none);
+  s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, c == 0, c0, c1, gamma, raw, none);
+  if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y)) {  // NaN / inf inputs: the reference's semantics
+    auto raw_t = [&](int t) {
+      return *reinterpret_cast<const uint32_t*>(xs + box_off(t, lane >> 2) + (lane & 3) * 4);
+    };
+    s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, c == 0, c0, c1, gamma, raw_t, none);
+  }
   const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
   *reinterpret_cast<float2*>(p.agg + n * kHD + j0) = s;
   if (lane == 0) p.A[n] = a;
@@ -335,11 +343,21 @@ __global__ void __launch_bounds__(kSpans * 32) p3_carry_kernel(const Params p) {
   // span aggregate: state after the span from zero, and its decay product
   float2 B = make_float2(0.f, 0.f);
   float A = 1.f;
-  for (int c = c0; c < c1; ++c) {
-    const float Ac = __ldg(p.A + n0 + c);
-    const float2 g = __ldg(reinterpret_cast<const float2*>(p.agg + (n0 + c) * kHD) + lane);
-    B = fma2(make_float2(Ac, Ac), B, g);
-    A *= Ac;
+  for (int cb = c0; cb < c1; cb += 8) {  // loads of 8 chunks first, then the fold
+    float Ac[8];
+    float2 g[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int cc = min(cb + q, c1 - 1);
+      Ac[q] = __ldg(p.A + n0 + cc);
+      g[q] = __ldg(reinterpret_cast<const float2*>(p.agg + (n0 + cc) * kHD) + lane);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (cb + q < c1) {
+        B = make_float2(fmaf(Ac[q], B.x, g[q].x), fmaf(Ac[q], B.y, g[q].y));
+        A *= Ac[q];
+      }
   }
   spanB[w][lane] = B;
   if (lane == 0) spanA[w] = A;
@@ -348,25 +366,66 @@ __global__ void __launch_bounds__(kSpans * 32) p3_carry_kernel(const Params p) {
     float2 X = make_float2(0.f, 0.f);
     for (int q = 0; q < kSpans; ++q) {
       spanX[q][lane] = X;
-      X = fma2(make_float2(spanA[q], spanA[q]), X, spanB[q][lane]);
+      X = make_float2(fmaf(spanA[q], X.x, spanB[q][lane].x), fmaf(spanA[q], X.y, spanB[q][lane].y));
     }
   }
   __syncthreads();
   float2 X = spanX[w][lane];
-  for (int c = c0; c < c1; ++c) {
-    reinterpret_cast<float2*>(p.carry + (n0 + c) * kHD)[lane] = X;
-    const float Ac = __ldg(p.A + n0 + c);
-    const float2 g = __ldg(reinterpret_cast<const float2*>(p.agg + (n0 + c) * kHD) + lane);
-    X = fma2(make_float2(Ac, Ac), X, g);
+  for (int cb = c0; cb < c1; cb += 8) {
+    float Ac[8];
+    float2 g[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int cc = min(cb + q, c1 - 1);
+      Ac[q] = __ldg(p.A + n0 + cc);
+      g[q] = __ldg(reinterpret_cast<const float2*>(p.agg + (n0 + cc) * kHD) + lane);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (cb + q < c1) {
+        reinterpret_cast<float2*>(p.carry + (n0 + cb + q) * kHD)[lane] = X;
+        X = make_float2(fmaf(Ac[q], X.x, g[q].x), fmaf(Ac[q], X.y, g[q].y));
+      }
   }
 }
 
 // ---------------------------------------------------------------------------
 // pass 3: outputs from the carries
 // ---------------------------------------------------------------------------
+// One chunk of one head: x and out with token strides XS / OS (elements;
+// compile-time when the tensors are contiguous, so every access is an
+// immediate offset), all 32 tokens (FULL) or the ragged last chunk.
+template <bool PRECISE, typename OT, typename Stride>
+OSSM_DEV float2 out_chunk(const __nv_bfloat16* xp, OT* op, Stride xs, Stride os, float2 X, const float2* lam, bool first,
+                          const float (&c0)[8], const float (&c1)[8], float gamma) {
+  uint32_t r[kL];
+#pragma unroll
+  for (int t = 0; t < kL; ++t) r[t] = __ldcs(reinterpret_cast<const unsigned int*>(xp + t * xs));
+  auto raw = [&](int t) { return r[t]; };
+  auto emit = [&](int t, float2 v) { st2(op + t * os, sizeof(OT) == 4 ? make_float2(clamp1(v.x), clamp1(v.y)) : v); };
+  float2 s = ema_chunk<PRECISE, false>(X, lam, first, c0, c1, gamma, raw, emit);
+  if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y)) {  // NaN / inf inputs: redo with the reference's semantics
+    auto reraw = [&](int t) { return __ldcs(reinterpret_cast<const unsigned int*>(xp + t * xs)); };
+    s = ema_chunk_exact<PRECISE>(X, lam, first, c0, c1, gamma, reraw, emit);
+  }
+  return s;
+}
+// The ragged last chunk (nt < 32 tokens), or strided tensors: a rolled loop
+// with the reference's semantics throughout.
 template <bool PRECISE, typename OT>
-__global__ void __launch_bounds__(kNT) p3_out_kernel(const Params p, const float* lam_tok) {
-  __shared__ float4 lam_s[kH * kL];
+OSSM_DEV float2 out_chunk_general(const __nv_bfloat16* xp, OT* op, long long xs, long long os, int nt, float2 X,
+                                  const float2* lam, bool first, const float (&c0)[8], const float (&c1)[8],
+                                  float gamma) {
+  auto raw = [&](int t) { return t < nt ? __ldcs(reinterpret_cast<const unsigned int*>(xp + t * xs)) : 0u; };
+  auto emit = [&](int t, float2 v) {
+    if (t < nt) st2(op + t * os, sizeof(OT) == 4 ? make_float2(clamp1(v.x), clamp1(v.y)) : v);
+  };
+  return ema_chunk_exact<PRECISE>(X, lam, first, c0, c1, gamma, raw, emit);
+}
+
+template <bool PRECISE, typename OT, bool CONTIG>
+__global__ void __launch_bounds__(kNT, 3) p3_out_kernel(const Params p, const float* lam_tok) {
+  __shared__ float2 lam_s[kH * kL];
   const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
   const int j0 = lane * 2, ch0 = h * kHD + j0;
   const int c = (int)(blockIdx.x / p.B), b = (int)(blockIdx.x % p.B);
@@ -374,12 +433,6 @@ __global__ void __launch_bounds__(kNT) p3_out_kernel(const Params p, const float
   const float gamma = 0.98f - 0.06f * (float)h / (float)kH;
   const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
 
-  // x of this chunk (L2 or HBM), the carry, the decays, the coefficients
-  const __nv_bfloat16* xp = p.x + (size_t)b * p.xsb + (size_t)t0 * p.xss + ch0;
-  uint32_t r[kL];
-#pragma unroll
-  for (int t = 0; t < kL; ++t)
-    r[t] = t < nt ? __ldcs(reinterpret_cast<const unsigned int*>(xp + (size_t)t * p.xss)) : 0u;
   float2 X;
   if (c == 0)
     X = p.init ? __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + ch0)) : make_float2(0.f, 0.f);
@@ -387,23 +440,20 @@ __global__ void __launch_bounds__(kNT) p3_out_kernel(const Params p, const float
     X = *reinterpret_cast<const float2*>(p.carry + n * kHD + j0);
   const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
   const float lam = lam_token(p, lam_tok, b, t0 + lane, h, lam_base);
-  lam_s[h * kL + lane] = make_float4(lam, lam, 1.f - lam, 1.f - lam);
-  float2 cf[8];
-  load_coeffs<PRECISE>(p, b, h, j0, gamma, cf);
+  lam_s[h * kL + lane] = make_float2(lam, 1.f - lam);
+  float c0[8], c1[8];
+  load_coeffs<PRECISE>(p, b, h, j0, gamma, c0, c1);
   __syncwarp();
 
+  const __nv_bfloat16* xp = p.x + (size_t)b * p.xsb + (size_t)t0 * p.xss + ch0;
   OT* op = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + (size_t)t0 * p.oss + ch0;
-  auto raw = [&](int t) { return r[t]; };
-  auto emit = [&](int t, float2 v) {
-    if (t < nt) st2(op + (size_t)t * p.oss, sizeof(OT) == 4 ? make_float2(clamp1(v.x), clamp1(v.y)) : v);
-  };
-  float2 s = ema_chunk<PRECISE, false>(X, lam_s + h * kL, c == 0, cf, gamma, raw, emit);
-  if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y)) {  // NaN / inf inputs: redo with the reference's semantics
-    auto reraw = [&](int t) {
-      return t < nt ? __ldcs(reinterpret_cast<const unsigned int*>(xp + (size_t)t * p.xss)) : 0u;
-    };
-    s = ema_chunk_exact<PRECISE>(X, lam_s + h * kL, c == 0, cf, gamma, reraw, emit);
-  }
+  float2 s;
+  if (nt < kL)
+    s = out_chunk_general<PRECISE, OT>(xp, op, p.xss, p.oss, nt, X, lam_s + h * kL, c == 0, c0, c1, gamma);
+  else if (CONTIG)
+    s = out_chunk<PRECISE, OT>(xp, op, kD, kD, X, lam_s + h * kL, c == 0, c0, c1, gamma);
+  else
+    s = out_chunk<PRECISE, OT>(xp, op, p.xss, p.oss, X, lam_s + h * kL, c == 0, c0, c1, gamma);
   // decays are 1 past the end, so the chunk's last state is the sequence's final state
   if (p.fin && t0 + kL >= p.S)
     *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) = make_float2(clamp1(s.x), clamp1(s.y));
@@ -420,7 +470,11 @@ cudaError_t launch_agg(const CUtensorMap& mx, const Params& p, cudaStream_t st) 
 
 template <bool PRECISE, typename OT>
 cudaError_t launch_out(const Params& p, const float* lam_tok, cudaStream_t st) {
-  p3_out_kernel<PRECISE, OT><<<p.B * p.nchunks, kNT, 0, st>>>(p, lam_tok);
+  const bool contig = p.xss == kD && p.oss == kD;  // token strides of x and out
+  if (contig)
+    p3_out_kernel<PRECISE, OT, true><<<p.B * p.nchunks, kNT, 0, st>>>(p, lam_tok);
+  else
+    p3_out_kernel<PRECISE, OT, false><<<p.B * p.nchunks, kNT, 0, st>>>(p, lam_tok);
   return cudaGetLastError();
 }
 
