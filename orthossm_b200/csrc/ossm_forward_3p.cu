@@ -23,9 +23,9 @@
 // a second evaluation and a second read of x.  Results are bitwise
 // reproducible (every fold has a fixed order).
 //
-// NaN and infinite inputs are handled off the hot path: the fast evaluation
-// lets them surface as NaN, each warp checks its chunk once and recomputes it
-// with the reference's semantics.
+// NaN inputs are handled off the hot path: the fast evaluation lets them
+// surface as NaN, each warp checks its chunk once and recomputes it with the
+// reference's semantics (u = 0 there).
 #include <cudaTypedefs.h>
 
 #include "ossm_sm100.cuh"
@@ -81,10 +81,14 @@ OSSM_DEV float clamp4_nan(float v) {  // NaN-propagating clamp to [-4, 4]
   asm("max.NaN.f32 %0, %1, 0fC0800000;\n\tmin.NaN.f32 %0, %0, 0f40800000;" : "=f"(r) : "f"(v));
   return r;
 }
-OSSM_DEV float rcp_approx(float x) {  // keeps subnormal results: huge |x| still gives x * rcp(1 + |x|) ~ 1
-  float y;
-  asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
+// x / (1 + |x|) with x first clamped to +-2^60 (NaN passes through): one
+// flush-to-zero reciprocal, exact enough for every finite bf16 input, and
+// +-inf gives +-1 as the reference's 1 - 1/(1 + |x|) does.
+OSSM_DEV float softsign_fast(float x) {
+  float xc, r;
+  asm("max.NaN.f32 %0, %1, 0fDD800000;\n\tmin.NaN.f32 %0, %0, 0f5D800000;" : "=f"(xc) : "f"(x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + fabsf(xc)));
+  return xc * r;
 }
 
 // Chebyshev -> monomial coefficients with gamma folded in (T_0..T_7 written out).
@@ -119,10 +123,10 @@ OSSM_DEV void load_coeffs(const Params& p, int b, int h, int j0, float gamma, fl
   for (int q = 0; q < 8; ++q) c0[q] = cf[q].x, c1[q] = cf[q].y;
 }
 
-// u = tanh(clamp(gamma y(xn), +-4)) for the lane's 2 channels of one token.
+// u = tanh(clamp(gamma y(xn), +-4)) for one channel of one token.
 // EXACT: the reference's semantics for every input (NaN -> u = 0,
-// sdpc_kernel.py:1164; +-inf -> xn = +-1, :1078-1085).  Otherwise NaN and
-// +-inf inputs come out as NaN (caught per chunk); every finite input takes the
+// sdpc_kernel.py:1164; +-inf -> xn = +-1, :1078-1085).  Otherwise a NaN input
+// comes out as NaN (caught per chunk); every other input takes the
 // reference's formula either way.
 template <bool PRECISE, bool EXACT>
 OSSM_DEV float eval_u1(float x, const float (&c)[8], float gamma) {
@@ -131,8 +135,8 @@ OSSM_DEV float eval_u1(float x, const float (&c)[8], float gamma) {
     float xa, sg;
     xn = softsign<PRECISE>(x, false, xa, sg);
     if (!EXACT && x != x) xn = x;
-  } else {  // x / (1 + |x|); inf / inf = NaN
-    xn = x * rcp_approx(1.0f + fabsf(x));
+  } else {
+    xn = softsign_fast(x);
   }
   float y;
   if (PRECISE) {  // Clenshaw on the raw coefficients, then gamma
@@ -166,8 +170,8 @@ OSSM_DEV float2 eval_u(uint32_t raw, const float (&c0)[8], const float (&c1)[8],
 // s <- l s + (1 - l) u; token 0 of the sequence (first) folds the carried-in
 // state with the reference's clamp.
 OSSM_DEV float2 ema_step(float2 s, float2 lm, float2 u, bool first) {  // lm = (l, 1 - l)
-  const float2 r = make_float2(fmaf(lm.x, s.x, lm.y * u.x), fmaf(lm.x, s.y, lm.y * u.y));
-  return first ? make_float2(clamp1(r.x), clamp1(r.y)) : r;
+  if (first) return make_float2(clamp1(fmaf(lm.x, s.x, lm.y * u.x)), clamp1(fmaf(lm.x, s.y, lm.y * u.y)));
+  return fma2(make_float2(lm.x, lm.x), s, mul2(make_float2(lm.y, lm.y), u));
 }
 
 // The 32-token EMA of one chunk from state s (decays lam[0..31]); RAW(t) gives
