@@ -130,6 +130,28 @@ int ossm_cheby_ema_fwd_noalloc(const ossm_fwd_args* a, ossm_stream_t stream, voi
  * configs[1] defines the per-token form. */
 int ossm_gate_decay(const ossm_fwd_args* a, float* lam_tok, ossm_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Sequence sharding (no counterpart in the reference,
+ * whose streaming loop is sequential, sdpc_kernel.py:2574-2606).  Rank r holds
+ * the consecutive tokens of shard r of every sequence in a->x (a->S = shard
+ * length).  Bf16 fast path only (bf16 x, 8 heads of 64); workspace as given by
+ * ossm_fwd_workspace_bytes(a).
+ *
+ *  1. ossm_fwd_shard_aggregate: chunk aggregates and carries of the shard from
+ *     a zero state (from a->init_state on the shard that starts the sequence),
+ *     and the shard's totals: shard_decay[b*H + h] = the product of the decays
+ *     over the shard, shard_state[b*D + d] = the state at its end.
+ *  2. The caller exchanges the totals (an all-gather of (B*H + B*D) floats per
+ *     rank) and folds the state entering its shard:
+ *     X_0 = init_state (or 0), X_{q+1} = shard_decay_q * X_q + shard_state_q.
+ *  3. ossm_fwd_shard_output: the shard's outputs (and final_state, the state
+ *     after its last token) from that carry_in [B*D] (ignored when
+ *     starts_sequence). */
+int ossm_fwd_shard_aggregate(const ossm_fwd_args* a, int starts_sequence, void* workspace, size_t workspace_bytes,
+                             float* shard_decay, float* shard_state, ossm_stream_t stream);
+int ossm_fwd_shard_output(const ossm_fwd_args* a, int starts_sequence, const float* carry_in, void* workspace,
+                          size_t workspace_bytes, ossm_stream_t stream);
+
 /* Read (and optionally clear) the sticky device status word of a workspace:
  * OSSM_OK, or OSSM_ETIMEOUT if a look-back wait gave up.  Synchronises the
  * stream. */

@@ -7,7 +7,8 @@ Public API mirrors the reference's ``sdpc_kernel`` op surface; see
 from .sdpc_kernel import (  # noqa: F401
     BASELINE_LAMBDA, LUT_TABLE_SIZE, MAX_DEGREE, MULTI_SCALE_LAMBDA, FusedChebyRKVv10,
     GatedComplexityPredictor, apply_cheby_rkv_core, apply_cheby_rkv_v10, cheby_ema_forward,
-    gate_decay, get_chebyshev_lut, init_chebyshev_coefficients, workspace_status,
+    cheby_ema_forward_seqpar, exchange_shard_totals, fold_shard_carries, gate_decay, get_chebyshev_lut,
+    init_chebyshev_coefficients, workspace_status,
 )
 
 __version__ = "0.1.0"

@@ -413,6 +413,9 @@ size_t ossm_tc_workspace_bytes(const ossm_fwd_args* a);
 int ossm_tc_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
 size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a);
 int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
+int ossm_p3_shard_front(const ossm_fwd_args* a, int starts_sequence, char* ws, float* shard_decay, float* shard_state,
+                        cudaStream_t st);
+int ossm_p3_shard_back(const ossm_fwd_args* a, int starts_sequence, const float* carry_in, char* ws, cudaStream_t st);
 
 namespace {
 
@@ -590,6 +593,39 @@ extern "C" int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_
     e = a->out_dtype == OSSM_F32 ? launch_fwd_dt<__nv_bfloat16, float>(p, precise, general, st)
                                  : launch_fwd_dt<__nv_bfloat16, __nv_bfloat16>(p, precise, general, st);
   return e == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
+}
+
+// Sequence-sharded forward (one shard of consecutive tokens per rank).  Only
+// the bf16 fast path (8 heads x 64) supports it; the workspace is the one
+// ossm_fwd_workspace_bytes gives for the shard's arguments.
+namespace {
+int shard_check(const ossm_fwd_args* a, void* workspace, size_t workspace_bytes) {
+  const int v = validate_fwd(a);
+  if (v != OSSM_OK) return v;
+  if (!ossm_tc_eligible(a) || (a->flags & OSSM_F_SINGLE_PASS)) return OSSM_EINVAL;
+  if (!workspace || workspace_bytes < ossm_p3_workspace_bytes(a) || ((uintptr_t)workspace % 256))
+    return OSSM_EWORKSPACE;
+  return OSSM_OK;
+}
+}  // namespace
+
+extern "C" int ossm_fwd_shard_aggregate(const ossm_fwd_args* a, int starts_sequence, void* workspace,
+                                        size_t workspace_bytes, float* shard_decay, float* shard_state,
+                                        ossm_stream_t stream) {
+  const int v = shard_check(a, workspace, workspace_bytes);
+  if (v != OSSM_OK) return v;
+  if (!shard_decay || !shard_state || ((uintptr_t)shard_state % 8)) return OSSM_EINVAL;
+  return ossm_p3_shard_front(a, starts_sequence, static_cast<char*>(workspace), shard_decay, shard_state,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ossm_fwd_shard_output(const ossm_fwd_args* a, int starts_sequence, const float* carry_in,
+                                     void* workspace, size_t workspace_bytes, ossm_stream_t stream) {
+  const int v = shard_check(a, workspace, workspace_bytes);
+  if (v != OSSM_OK) return v;
+  if (!starts_sequence && (!carry_in || ((uintptr_t)carry_in % 8))) return OSSM_EINVAL;
+  return ossm_p3_shard_back(a, starts_sequence, carry_in, static_cast<char*>(workspace),
+                            reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ossm_gate_decay(const ossm_fwd_args* a, float* lam_tok, ossm_stream_t stream) {

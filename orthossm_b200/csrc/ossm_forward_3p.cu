@@ -72,8 +72,13 @@ struct Params {
   long long osb, oss;
   float* A;      // [N] chunk decay products
   float* agg;    // [N][64] chunk end states from zero (chunk 0: from the carried-in state)
-  float* carry;  // [N][64] state entering each chunk
+  float* carry;  // [N][64] state entering each chunk (from a zero state at the shard start)
+  float* P;      // [N] decay product from the shard start to each chunk's start
   WsHeader* ws;  // sticky status (a tile that never arrived)
+  int starts_seq;         // this call's first token is token 0 of the sequence
+  float* tot_A;           // [B*H] shard decay products (or NULL)
+  float* tot_E;           // [B*H][64] shard end states from a zero state (or NULL)
+  const float* carry_in;  // [B][D] state entering the shard (or NULL: zero / init_state)
 };
 
 OSSM_DEV float clamp4_nan(float v) {  // NaN-propagating clamp to [-4, 4]
@@ -305,14 +310,15 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
     if (tg < p.S) p.lam_ws[((size_t)b * p.S + tg) * kH + h] = lam;  // for the output pass
     else lam = 1.f;
   }
-  float a = tg == 0 ? 0.f : lam;  // the chunk's decay product (the carry enters at token 0)
+  const bool first = c == 0 && p.starts_seq;  // token 0 of the sequence: the carried-in state enters here
+  float a = (first && lane == 0) ? 0.f : lam;  // the chunk's decay product
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) a *= __shfl_xor_sync(0xffffffffu, a, o);
   lam_s[h * kL + lane] = make_float2(lam, 1.f - lam);
   __syncwarp();
 
   float2 s = make_float2(0.f, 0.f);
-  if (c == 0 && p.init) s = __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + h * kHD + j0));
+  if (first && p.init) s = __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + h * kHD + j0));
   const float2 s_in = s;
   // the lane's 4 bytes of token t sit at t*128 + ((lane/4 ^ t%8) * 16) + (lane%4)*4: 8 row patterns
   uint32_t roff[8];
@@ -320,12 +326,12 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
   for (int k = 0; k < 8; ++k) roff[k] = (uint32_t)((((lane >> 2) ^ k) << 4) + (lane & 3) * 4);
   auto raw = [&](int t) { return *reinterpret_cast<const uint32_t*>(xs + roff[t & 7] + t * 128); };
   auto none = [](int, float2) {};
-  s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, c == 0, c0, c1, gamma, raw, none);
+  s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, first, c0, c1, gamma, raw, none);
   if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y)) {  // NaN / inf inputs: the reference's semantics
     auto raw_t = [&](int t) {
       return *reinterpret_cast<const uint32_t*>(xs + box_off(t, lane >> 2) + (lane & 3) * 4);
     };
-    s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, c == 0, c0, c1, gamma, raw_t, none);
+    s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, first, c0, c1, gamma, raw_t, none);
   }
   const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
   *reinterpret_cast<float2*>(p.agg + n * kHD + j0) = s;
@@ -340,6 +346,7 @@ __global__ void __launch_bounds__(kSpans * 32) p3_carry_kernel(const Params p) {
   __shared__ float2 spanB[kSpans][32];
   __shared__ float spanA[kSpans];
   __shared__ float2 spanX[kSpans][32];
+  __shared__ float spanP[kSpans];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t n0 = (size_t)blockIdx.x * p.nchunks;
   const int per = (p.nchunks + kSpans - 1) / kSpans;
@@ -366,15 +373,21 @@ __global__ void __launch_bounds__(kSpans * 32) p3_carry_kernel(const Params p) {
   spanB[w][lane] = B;
   if (lane == 0) spanA[w] = A;
   __syncthreads();
-  if (w == 0) {  // carries into the spans, in span order
+  if (w == 0) {  // carries into the spans, in span order; the chain's totals
     float2 X = make_float2(0.f, 0.f);
+    float P = 1.f;
     for (int q = 0; q < kSpans; ++q) {
       spanX[q][lane] = X;
+      spanP[q] = P;
       X = make_float2(fmaf(spanA[q], X.x, spanB[q][lane].x), fmaf(spanA[q], X.y, spanB[q][lane].y));
+      P *= spanA[q];
     }
+    if (p.tot_E) reinterpret_cast<float2*>(p.tot_E + (size_t)blockIdx.x * kHD)[lane] = X;
+    if (p.tot_A && lane == 0) p.tot_A[blockIdx.x] = P;
   }
   __syncthreads();
   float2 X = spanX[w][lane];
+  float Pc = spanP[w];
   for (int cb = c0; cb < c1; cb += 8) {
     float Ac[8];
     float2 g[8];
@@ -388,7 +401,9 @@ __global__ void __launch_bounds__(kSpans * 32) p3_carry_kernel(const Params p) {
     for (int q = 0; q < 8; ++q)
       if (cb + q < c1) {
         reinterpret_cast<float2*>(p.carry + (n0 + cb + q) * kHD)[lane] = X;
+        if (lane == 0) p.P[n0 + cb + q] = Pc;
         X = make_float2(fmaf(Ac[q], X.x, g[q].x), fmaf(Ac[q], X.y, g[q].y));
+        Pc *= Ac[q];
       }
   }
 }
@@ -437,11 +452,18 @@ __global__ void __launch_bounds__(kNT, 3) p3_out_kernel(const Params p, const fl
   const float gamma = 0.98f - 0.06f * (float)h / (float)kH;
   const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
 
+  const bool first = c == 0 && p.starts_seq;
   float2 X;
-  if (c == 0)
+  if (first) {
     X = p.init ? __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + ch0)) : make_float2(0.f, 0.f);
-  else
-    X = *reinterpret_cast<const float2*>(p.carry + n * kHD + j0);
+  } else {
+    X = c == 0 ? make_float2(0.f, 0.f) : *reinterpret_cast<const float2*>(p.carry + n * kHD + j0);
+    if (p.carry_in) {  // the state entering the shard, decayed to this chunk
+      const float Pn = c == 0 ? 1.f : p.P[n];
+      const float2 ci = __ldg(reinterpret_cast<const float2*>(p.carry_in + (size_t)b * kD + ch0));
+      X = make_float2(fmaf(Pn, ci.x, X.x), fmaf(Pn, ci.y, X.y));
+    }
+  }
   const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
   const float lam = lam_token(p, lam_tok, b, t0 + lane, h, lam_base);
   lam_s[h * kL + lane] = make_float2(lam, 1.f - lam);
@@ -453,11 +475,11 @@ __global__ void __launch_bounds__(kNT, 3) p3_out_kernel(const Params p, const fl
   OT* op = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + (size_t)t0 * p.oss + ch0;
   float2 s;
   if (nt < kL)
-    s = out_chunk_general<PRECISE, OT>(xp, op, p.xss, p.oss, nt, X, lam_s + h * kL, c == 0, c0, c1, gamma);
+    s = out_chunk_general<PRECISE, OT>(xp, op, p.xss, p.oss, nt, X, lam_s + h * kL, first, c0, c1, gamma);
   else if (CONTIG)
-    s = out_chunk<PRECISE, OT>(xp, op, kD, kD, X, lam_s + h * kL, c == 0, c0, c1, gamma);
+    s = out_chunk<PRECISE, OT>(xp, op, kD, kD, X, lam_s + h * kL, first, c0, c1, gamma);
   else
-    s = out_chunk<PRECISE, OT>(xp, op, p.xss, p.oss, X, lam_s + h * kL, c == 0, c0, c1, gamma);
+    s = out_chunk<PRECISE, OT>(xp, op, p.xss, p.oss, X, lam_s + h * kL, first, c0, c1, gamma);
   // decays are 1 past the end, so the chunk's last state is the sequence's final state
   if (p.fin && t0 + kL >= p.S)
     *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) = make_float2(clamp1(s.x), clamp1(s.y));
@@ -487,20 +509,21 @@ cudaError_t launch_out(const Params& p, const float* lam_tok, cudaStream_t st) {
 
 using namespace ossm;
 
-// Workspace of the three-pass path: header, decay products, aggregates,
-// carries and (gated) the per-token decays.
+// Workspace of the three-pass path: header, decay products, prefix products,
+// aggregates, carries and (gated) the per-token decays.
 size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a) {
   const size_t nch = (size_t)(a->S + p3::kL - 1) / p3::kL;
   const size_t N = (size_t)a->B * p3::kH * nch;
   auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
-  size_t bytes = al(sizeof(WsHeader)) + al(N * 4) + 2 * al(N * p3::kHD * 4);
+  size_t bytes = al(sizeof(WsHeader)) + 2 * al(N * 4) + 2 * al(N * p3::kHD * 4);
   if (a->gate_w && !a->lam_tok) bytes += al((size_t)a->B * a->S * p3::kH * 4);
   return bytes;
 }
 
-int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
+namespace {
+
+int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
   using namespace p3;
-  Params p;
   p.B = a->B;
   p.S = a->S;
   p.K = (a->flags & OSSM_EVAL_MASK) == OSSM_EVAL_CLENSHAW_DEG4 ? (a->degree < 4 ? a->degree : 4) : a->degree;
@@ -511,7 +534,6 @@ int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
   p.coeffs = a->coeffs;
   p.lam_h = a->lam_h;
   p.momentum = a->momentum;
-  const bool gate = a->gate_w && !a->lam_tok;
   p.gate_w = a->gate_w;
   p.gate_b = a->gate_b;
   p.gate_scale = a->gate_scale;
@@ -523,21 +545,34 @@ int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
   p.out = a->out;
   p.osb = a->out_stride_b;
   p.oss = a->out_stride_s;
+  const bool gate = a->gate_w && !a->lam_tok;
   const size_t N = (size_t)a->B * kH * p.nchunks;
   auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
   p.ws = reinterpret_cast<WsHeader*>(ws);
   size_t off = al(sizeof(WsHeader));
   p.A = reinterpret_cast<float*>(ws + off);
   off += al(N * 4);
+  p.P = reinterpret_cast<float*>(ws + off);
+  off += al(N * 4);
   p.agg = reinterpret_cast<float*>(ws + off);
   off += al(N * kHD * 4);
   p.carry = reinterpret_cast<float*>(ws + off);
   off += al(N * kHD * 4);
   p.lam_ws = gate ? reinterpret_cast<float*>(ws + off) : nullptr;
+  p.starts_seq = 1;
+  p.tot_A = nullptr;
+  p.tot_E = nullptr;
+  p.carry_in = nullptr;
   if ((long long)a->B * p.nchunks > 0x7fffffffLL) return OSSM_EINVAL;
+  return OSSM_OK;
+}
 
+// passes 1 and 2: aggregates, carries (and the shard totals when asked)
+int p3_front(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
+  using namespace p3;
   CUtensorMap mx;
   if (!fast::encode_map(&mx, a->x, a->S, a->B, a->x_stride_s, a->x_stride_b)) return OSSM_EINVAL;
+  const bool gate = a->gate_w && !a->lam_tok;
   const bool precise = (a->out_dtype == OSSM_F32) || (a->flags & OSSM_F_PRECISE);
   cudaError_t e;
   if (precise)
@@ -546,11 +581,49 @@ int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
     e = gate ? launch_agg<true, false>(mx, p, st) : launch_agg<false, false>(mx, p, st);
   if (e != cudaSuccess) return OSSM_ELAUNCH;
   p3_carry_kernel<<<a->B * kH, kSpans * 32, 0, st>>>(p);
-  if ((e = cudaGetLastError()) != cudaSuccess) return OSSM_ELAUNCH;
+  return cudaGetLastError() == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
+}
+
+// pass 3: outputs
+int p3_back(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
+  using namespace p3;
+  const bool gate = a->gate_w && !a->lam_tok;
+  const bool precise = (a->out_dtype == OSSM_F32) || (a->flags & OSSM_F_PRECISE);
   const float* lam_tok = gate ? p.lam_ws : a->lam_tok;
+  cudaError_t e;
   if (a->out_dtype == OSSM_F32)
     e = launch_out<true, float>(p, lam_tok, st);
   else
     e = precise ? launch_out<true, __nv_bfloat16>(p, lam_tok, st) : launch_out<false, __nv_bfloat16>(p, lam_tok, st);
   return e == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
+}
+
+}  // namespace
+
+int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
+  p3::Params p;
+  int r = p3_params(a, ws, p);
+  if (r != OSSM_OK) return r;
+  if ((r = p3_front(a, p, st)) != OSSM_OK) return r;
+  return p3_back(a, p, st);
+}
+
+int ossm_p3_shard_front(const ossm_fwd_args* a, int starts_sequence, char* ws, float* shard_decay, float* shard_state,
+                        cudaStream_t st) {
+  p3::Params p;
+  int r = p3_params(a, ws, p);
+  if (r != OSSM_OK) return r;
+  p.starts_seq = starts_sequence ? 1 : 0;
+  p.tot_A = shard_decay;
+  p.tot_E = shard_state;
+  return p3_front(a, p, st);
+}
+
+int ossm_p3_shard_back(const ossm_fwd_args* a, int starts_sequence, const float* carry_in, char* ws, cudaStream_t st) {
+  p3::Params p;
+  int r = p3_params(a, ws, p);
+  if (r != OSSM_OK) return r;
+  p.starts_seq = starts_sequence ? 1 : 0;
+  p.carry_in = starts_sequence ? nullptr : carry_in;
+  return p3_back(a, p, st);
 }

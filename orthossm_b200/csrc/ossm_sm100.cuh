@@ -1,5 +1,5 @@
 // sm_100a primitives used by the TMA / tcgen05 forward: mbarriers, bulk tensor
-// copies (no multicast anywhere), clusters / distributed shared memory, and
+// copies (each into this CTA's own shared memory), clusters / distributed shared memory, and
 // tcgen05 MMA with TMEM accumulators.  Inline PTX only.
 #pragma once
 
@@ -39,7 +39,7 @@ OSSM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-// ---------------------------------------------------------------- TMA (tiled, no multicast)
+// ---------------------------------------------------------------- TMA (tiled, CTA-local destinations)
 OSSM_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
@@ -47,7 +47,7 @@ OSSM_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int 
       : "memory");
 }
 // 1D bulk copy global -> shared (16-byte aligned, size a multiple of 16),
-// completing on an mbarrier transaction count.  No multicast.
+// completing on an mbarrier transaction count (CTA-local destination).
 OSSM_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))

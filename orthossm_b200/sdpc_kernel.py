@@ -154,24 +154,12 @@ def _rowmajor(x):
 # BASELINE-semantics forward
 # ----------------------------------------------------------------------------
 
-def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,
-                      gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None,
-                      out_dtype=None, return_tanh=False, eval_mode="clenshaw",
-                      fast_path_semantics=False, precise=None, out=None, final_state=None,
-                      lam_tok=None, force_generic=False):
-    """Fused softsign -> degree-K Chebyshev -> gamma_h -> tanh -> lambda-EMA.
-
-    x: [B,S,D] float32 or bfloat16 (CUDA); coeffs: [B,H,K,hd] float32.
-    lambda_per_head: [H] decay per head (None: scalar ``ema_momentum``).
-    gate_weight [H,D] / gate_bias [H]: per-token decay
-    ``clamp(lambda_h + gate_scale*(sigmoid(W x_t + b) - 0.5), *gate_range)``.
-    init_state: [B,D] float32 carried-in EMA state (None: zeros).
-    lam_tok: optional precomputed per-token decay [B,S,H] float32 (e.g. from
-    ``gate_decay``); overrides the gate.
-    force_generic: run the generic kernel even where the TMA / tcgen05 path
-    applies (bf16 x, head_dim 64); both compute the same function.
-    Returns (out [B,S,D] in out_dtype (default x.dtype), final_state [B,D] f32)
-    and the f32 tanh cache when ``return_tanh``."""
+def _fwd_args(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None, gate_bias=None,
+              gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None, out_dtype=None, return_tanh=False,
+              eval_mode="clenshaw", fast_path_semantics=False, precise=None, out=None, final_state=None,
+              lam_tok=None, force_generic=False):
+    """ossm_fwd_args for a forward call; returns (args, tensors to keep alive,
+    out, final_state)."""
     _need_cuda(x, coeffs)
     x = _rowmajor(x)
     if x.dtype not in _DT:
@@ -222,6 +210,36 @@ def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate
                   lut=_ptr(lut), init_state=_ptr(init_state), final_state=_ptr(final_state),
                   out=out.data_ptr(), out_dtype=_DT[out.dtype], out_stride_b=out.stride(0),
                   out_stride_s=out.stride(1), tanh_out=_ptr(tanh), lam_tok=_ptr(lam_tok), flags=flags)
+    keep = (x, coeffs, lam, gate_weight, gate_bias, init_state, lam_tok, tanh, lut)
+    return a, keep, out, final_state
+
+
+def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,
+                      gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None,
+                      out_dtype=None, return_tanh=False, eval_mode="clenshaw",
+                      fast_path_semantics=False, precise=None, out=None, final_state=None,
+                      lam_tok=None, force_generic=False):
+    """Fused softsign -> degree-K Chebyshev -> gamma_h -> tanh -> lambda-EMA.
+
+    x: [B,S,D] float32 or bfloat16 (CUDA); coeffs: [B,H,K,hd] float32.
+    lambda_per_head: [H] decay per head (None: scalar ``ema_momentum``).
+    gate_weight [H,D] / gate_bias [H]: per-token decay
+    ``clamp(lambda_h + gate_scale*(sigmoid(W x_t + b) - 0.5), *gate_range)``.
+    init_state: [B,D] float32 carried-in EMA state (None: zeros).
+    lam_tok: optional precomputed per-token decay [B,S,H] float32 (e.g. from
+    ``gate_decay``); overrides the gate.
+    force_generic: run the generic kernel even where the TMA / tcgen05 path
+    applies (bf16 x, head_dim 64); both compute the same function.
+    Returns (out [B,S,D] in out_dtype (default x.dtype), final_state [B,D] f32)
+    and the f32 tanh cache when ``return_tanh``."""
+    a, keep, out, final_state = _fwd_args(
+        x, coeffs, lambda_per_head=lambda_per_head, ema_momentum=ema_momentum, gate_weight=gate_weight,
+        gate_bias=gate_bias, gate_scale=gate_scale, gate_range=gate_range, init_state=init_state,
+        out_dtype=out_dtype, return_tanh=return_tanh, eval_mode=eval_mode,
+        fast_path_semantics=fast_path_semantics, precise=precise, out=out, final_state=final_state,
+        lam_tok=lam_tok, force_generic=force_generic)
+    tanh = keep[7]
+    dev = out.device
     lib = L.lib()
     nbytes = lib.ossm_fwd_workspace_bytes(L.C.byref(a))
     if nbytes == 0:
@@ -233,6 +251,84 @@ def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate
     if return_tanh:
         return out, final_state, tanh
     return out, final_state
+
+
+# ----------------------------------------------------------------------------
+# sequence sharding across ranks
+# ----------------------------------------------------------------------------
+
+def fold_shard_carries(decays, states, upto, init=None):
+    """State entering shard ``upto`` from every earlier shard's totals.
+
+    decays[q]: [B, H] decay product over shard q; states[q]: [B, D] state at
+    the end of shard q from a zero state (shard 0: from ``init``).  Folds
+    X_0 = init (or 0), X_{q+1} = decays[q] * X_q + states[q] in rank order, so
+    every rank computes bitwise the same carries.  Pure torch: runs on any
+    device (the multi-rank tests run it on CPU under gloo)."""
+    B, D = states[0].shape
+    H = decays[0].shape[-1]
+    X = torch.zeros(B, D, dtype=torch.float32, device=states[0].device) if init is None else init.float().clone()
+    for q in range(upto):
+        dq = decays[q].reshape(B, H, 1).expand(B, H, D // H).reshape(B, D)
+        X = torch.addcmul(states[q].reshape(B, D), dq, X)
+    return X
+
+
+def exchange_shard_totals(decay, state, group=None):
+    """All-gather every rank's shard totals (one collective per tensor)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    decays = [torch.empty_like(decay) for _ in range(world)]
+    states = [torch.empty_like(state) for _ in range(world)]
+    dist.all_gather(decays, decay.contiguous(), group=group)
+    dist.all_gather(states, state.contiguous(), group=group)
+    return decays, states
+
+
+def cheby_ema_forward_seqpar(x, coeffs, *, group=None, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,
+                             gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None,
+                             eval_mode="clenshaw", precise=None, out=None):
+    """``cheby_ema_forward`` over a sequence sharded across the ranks of
+    ``group`` (torch.distributed, one GPU per rank): rank r holds tokens
+    [r*S_shard, (r+1)*S_shard) of every sequence as ``x`` [B, S_shard, D]
+    (bf16, 8 heads of 64).  Each rank scans its shard, one all-gather
+    exchanges the shard totals ((H + D) floats per sequence per rank), each
+    rank folds the state entering its shard and writes its outputs.
+
+    ``init_state`` is the state before token 0 (used by rank 0; pass the same
+    tensor or None on every rank).  Returns (out [B, S_shard, D] bf16,
+    final_state [B, D] f32, the state after the last token of the whole
+    sequence, identical on every rank)."""
+    import torch.distributed as dist
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    _need_cuda(x, coeffs)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("cheby_ema_forward_seqpar: x must be bfloat16 (the fast path)")
+    a, keep, out, fin = _fwd_args(x, coeffs, lambda_per_head=lambda_per_head, ema_momentum=ema_momentum,
+                                  gate_weight=gate_weight, gate_bias=gate_bias, gate_scale=gate_scale,
+                                  gate_range=gate_range, init_state=init_state if rank == 0 else None,
+                                  out_dtype=torch.bfloat16, eval_mode=eval_mode, precise=precise, out=out)
+    B, S, D = x.shape
+    H = coeffs.shape[1]
+    dev = x.device
+    lib = L.lib()
+    nbytes = lib.ossm_fwd_workspace_bytes(L.C.byref(a))
+    if nbytes == 0:
+        L.check(L.OSSM_EINVAL, "cheby_ema_forward_seqpar (argument check)")
+    stream = torch.cuda.current_stream(dev)
+    ws = _workspace(dev, stream, nbytes)
+    decay = torch.empty(B, H, device=dev, dtype=torch.float32)
+    state = torch.empty(B, D, device=dev, dtype=torch.float32)
+    L.check(lib.ossm_fwd_shard_aggregate(L.C.byref(a), int(rank == 0), ws.data_ptr(), ws.numel(), decay.data_ptr(),
+                                         state.data_ptr(), stream.cuda_stream), "shard aggregate")
+    decays, states = exchange_shard_totals(decay, state, group)
+    init = None if init_state is None else init_state.to(dev, torch.float32)
+    carry_in = fold_shard_carries(decays, states, rank, init).contiguous()
+    L.check(lib.ossm_fwd_shard_output(L.C.byref(a), int(rank == 0), carry_in.data_ptr(), ws.data_ptr(), ws.numel(),
+                                      stream.cuda_stream), "shard output")
+    final = fold_shard_carries(decays, states, world, init)
+    del keep
+    return out, final
 
 
 def gate_decay(x, gate_weight, gate_bias, lambda_per_head, *, gate_scale=0.008,

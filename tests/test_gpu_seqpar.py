@@ -1,0 +1,141 @@
+"""Sequence sharding on the GPU, through the C ABI (ossm_fwd_shard_aggregate /
+ossm_fwd_shard_output) and through ``cheby_ema_forward_seqpar``.
+
+* one GPU: the sequence is cut into G shards that run one after another on
+  the same device, with the carry folded on the host side in between; the
+  joined outputs must match the unsharded forward and the oracle;
+* two GPUs (skipped when the box has one): two NCCL ranks, each with its
+  shard, against the unsharded forward."""
+import ctypes as C
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import cheby_ref as R
+from orthossm_b200 import _lib as L
+from tests.golden.inputs import det_normal, linear_init, spectral_coeffs
+from tests.test_oracle_golden import relerr
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dt=torch.float32, dev="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev, dt)
+
+
+def _problem(B, S, seed):
+    D, H = 512, 8
+    x = R.bf16_round(det_normal((B, S, D), seed)).astype(np.float32)
+    c = spectral_coeffs(B, H, 8, 64, seed + 1)
+    W, b = linear_init(H, D, seed + 2)
+    init = det_normal((B, D), seed + 3, 0.1)
+    lam = np.asarray(R.BASELINE_LAMBDA, np.float32)
+    return x, c, W, b, init, lam
+
+
+@pytest.mark.parametrize("B,S,G,gate", [(2, 4096, 2, True), (1, 3000, 4, True), (2, 2048, 4, False),
+                                        (1, 40000, 8, True)])
+def test_shards_on_one_gpu_match_unsharded(B, S, G, gate):
+    import orthossm_b200 as O
+    from orthossm_b200.sdpc_kernel import _fwd_args, fold_shard_carries
+    x, c, W, b, init, lam = _problem(B, S, 900 + S + G)
+    xb = _t(x, torch.bfloat16)
+    kw = dict(lambda_per_head=lam.tolist())
+    if gate:
+        kw.update(gate_weight=_t(W), gate_bias=_t(b))
+    full, fin_full = O.cheby_ema_forward(xb, _t(c), init_state=_t(init), **kw)
+    lib = L.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    bounds = [S * r // G for r in range(G + 1)]
+    outs, decays, states, calls = [], [], [], []
+    for r in range(G):
+        xs = xb[:, bounds[r]:bounds[r + 1]].contiguous()
+        a, keep, out, fin = _fwd_args(xs, _t(c), init_state=_t(init) if r == 0 else None,
+                                      out_dtype=torch.bfloat16, **kw)
+        nb = lib.ossm_fwd_workspace_bytes(C.byref(a))
+        ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+        dec = torch.empty(B, 8, device="cuda")
+        st = torch.empty(B, 512, device="cuda")
+        assert lib.ossm_fwd_shard_aggregate(C.byref(a), int(r == 0), ws.data_ptr(), nb, dec.data_ptr(),
+                                            st.data_ptr(), stream) == L.OSSM_OK
+        decays.append(dec)
+        states.append(st)
+        calls.append((a, keep, out, fin, ws, nb, xs))
+    for r, (a, keep, out, fin, ws, nb, xs) in enumerate(calls):
+        carry = fold_shard_carries(decays, states, r, _t(init)).contiguous()
+        assert lib.ossm_fwd_shard_output(C.byref(a), int(r == 0), carry.data_ptr(), ws.data_ptr(), nb,
+                                         stream) == L.OSSM_OK
+        outs.append(out)
+    torch.cuda.synchronize()
+    joined = torch.cat(outs, dim=1).float().cpu().numpy()
+    ref = full.float().cpu().numpy()
+    assert np.abs(joined - ref).max() <= 2 ** -7
+    fin_fold = fold_shard_carries(decays, states, G, _t(init)).cpu().numpy()
+    assert relerr(fin_fold, fin_full.cpu().numpy()) < 1e-5
+    assert relerr(calls[-1][3].cpu().numpy(), fin_full.cpu().numpy()) < 1e-5  # last shard's own final state
+    o = R.cheby_ema_forward(x, c, lam=lam.astype(np.float64), gate=dict(W=W, b=b) if gate else None, init=init)
+    assert relerr(joined, o["out"]) < 2e-2
+    assert O.workspace_status() == 0
+
+
+def test_shard_entry_points_reject_other_paths():
+    """fp32 x (the generic kernel) has no sharded path: EINVAL, nothing launched."""
+    from orthossm_b200.sdpc_kernel import _fwd_args
+    x, c, W, b, init, lam = _problem(1, 256, 5)
+    a, keep, out, fin = _fwd_args(_t(x), _t(c), lambda_per_head=lam.tolist())
+    lib = L.lib()
+    nb = lib.ossm_fwd_workspace_bytes(C.byref(a))
+    ws = torch.zeros(max(nb, 1 << 20), dtype=torch.uint8, device="cuda")
+    dec = torch.empty(1, 8, device="cuda")
+    st = torch.empty(1, 512, device="cuda")
+    assert lib.ossm_fwd_shard_aggregate(C.byref(a), 1, ws.data_ptr(), ws.numel(), dec.data_ptr(), st.data_ptr(),
+                                        None) == L.OSSM_EINVAL
+
+
+def _nccl_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import orthossm_b200 as O
+        B, S = 2, 8192
+        x, c, W, b, init, lam = _problem(B, S, 4242)
+        dev = f"cuda:{rank}"
+        kw = dict(lambda_per_head=lam.tolist(), gate_weight=_t(W, dev=dev), gate_bias=_t(b, dev=dev))
+        xb = _t(x, torch.bfloat16, dev)
+        full, fin_full = O.cheby_ema_forward(xb, _t(c, dev=dev), init_state=_t(init, dev=dev), **kw)
+        L_ = S // world
+        xs = xb[:, rank * L_:(rank + 1) * L_].contiguous()
+        out, fin = O.cheby_ema_forward_seqpar(xs, _t(c, dev=dev), init_state=_t(init, dev=dev), **kw)
+        torch.cuda.synchronize()
+        err = (out.float() - full[:, rank * L_:(rank + 1) * L_].float()).abs().max().item()
+        ferr = relerr(fin.cpu().numpy(), fin_full.cpu().numpy())
+        q.put((rank, err, ferr))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpus_nccl_match_unsharded():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, err, ferr in res:
+        assert err <= 2 ** -7, (rank, err)
+        assert ferr < 1e-5, (rank, ferr)
