@@ -304,7 +304,7 @@ def run_ours(args):
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
         try:
-            traffic = json.load(open(tp)).get("fwd_step_cfg2_bytes_per_launch")
+            traffic = json.load(open(tp)).get("fwd_step_cfg2_bytes_per_step")
         except Exception:
             traffic = None
 
@@ -357,8 +357,8 @@ def run_ours(args):
             "hbm_gbs_step": (elem * 4 + B * D * 8) / (ms / K_eff / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "forward step: p3_agg_kernel (gate + chunk aggregates) + p3_carry_kernel + p3_out_kernel", "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
-                         "peak_kind": peak_kind, "bytes_per_launch": scan_bytes,
-                         "avg_launch_ms": scan_avg},
+                         "peak_kind": peak_kind, "bytes_per_step": scan_bytes,
+                         "avg_step_ms": scan_avg},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": elem * 2,
                     "d2h_bytes_per_step": elem * 2 + B * D * 4},
             "clocks": clocks,
