@@ -187,12 +187,45 @@ typedef struct {
 
 int ossm_cheby_rkv_lion(const ossm_lion_args* a, ossm_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * BASELINE-mode TTT step for one chunk (no
+ * counterpart kernel in the reference, whose TTT is the local gated-error Lion
+ * step of sdpc_kernel.py:2126-2287).  Inputs: the chunk's x, its coefficients
+ * (those the forward used), the per-token decays, and
+ * gs = dL/ds = (2/N) W_pred^T (W_pred s_t - x_{t+1}) for t < L-1 ([B,L-1,D]
+ * fp32, contiguous; the caller forms it with two GEMMs).  Runs the reverse EMA
+ * adjoint, dy = (1-a_t) adj_t (1-u_t^2) gamma_h [|z_t| < 4], the gradient
+ * g_k = sum_t dy_t T_k(xn_t) / (k+1)^spectral_pow, and Adam on coeffs / m / v
+ * in place: c <- lam_h c - lr mhat / (sqrt(vhat) + eps) (lam_h = 1 when
+ * forget == 0), with bias corrections for Adam step `step` (>= 1).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  int32_t B, L, H, head_dim, degree; /* head_dim <= 64, degree <= 8 */
+  const void* x;                     /* [B,L,H*head_dim] */
+  int32_t x_dtype;
+  int64_t x_stride_b, x_stride_s;
+  float* coeffs;                     /* [B,H,degree,head_dim], in/out */
+  float* m;                          /* Adam first moment, same shape, in/out */
+  float* v;                          /* Adam second moment, same shape, in/out */
+  const float* lam_h;                /* [H] or NULL (momentum) */
+  float momentum;
+  const float* lam_tok;              /* [B,L,H] per-token decays or NULL (lam_h) */
+  const float* gs;                   /* [B,L-1,H*head_dim] fp32 */
+  float lr, beta1, beta2, eps, spectral_pow;
+  int32_t step;                      /* Adam step number of this update, >= 1 */
+  int32_t forget;                    /* 1: forget gate lam_h on c */
+} ossm_ttt_args;
+
+size_t ossm_ttt_workspace_bytes(const ossm_ttt_args* a);
+int ossm_ttt_wpred_step(const ossm_ttt_args* a, void* workspace, size_t workspace_bytes, ossm_stream_t stream);
+
 /* Library metadata. */
 const char* ossm_version(void);
 const char* ossm_status_string(int status);
 /* sizeof() of the argument structs, so bindings can check their layout. */
 size_t ossm_sizeof_fwd_args(void);
 size_t ossm_sizeof_lion_args(void);
+size_t ossm_sizeof_ttt_args(void);
 
 #ifdef __cplusplus
 }

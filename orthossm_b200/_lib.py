@@ -24,7 +24,8 @@ EXPORTED = (
     "ossm_fwd_workspace_bytes", "ossm_cheby_ema_fwd", "ossm_cheby_ema_fwd_noalloc", "ossm_gate_decay",
     "ossm_workspace_status", "ossm_fwd_shard_aggregate", "ossm_fwd_shard_output",
     "ossm_cheby_rkv_lion", "ossm_version", "ossm_status_string",
-    "ossm_sizeof_fwd_args", "ossm_sizeof_lion_args",
+    "ossm_sizeof_fwd_args", "ossm_sizeof_lion_args", "ossm_sizeof_ttt_args",
+    "ossm_ttt_workspace_bytes", "ossm_ttt_wpred_step",
 )
 
 _vp = C.c_void_p
@@ -57,6 +58,16 @@ class LionArgs(C.Structure):
     ]
 
 
+class TttArgs(C.Structure):
+    _fields_ = [
+        ("B", _i32), ("L", _i32), ("H", _i32), ("head_dim", _i32), ("degree", _i32),
+        ("x", _vp), ("x_dtype", _i32), ("x_stride_b", _i64), ("x_stride_s", _i64),
+        ("coeffs", _vp), ("m", _vp), ("v", _vp), ("lam_h", _vp), ("momentum", _f32), ("lam_tok", _vp),
+        ("gs", _vp), ("lr", _f32), ("beta1", _f32), ("beta2", _f32), ("eps", _f32), ("spectral_pow", _f32),
+        ("step", _i32), ("forget", _i32),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -83,7 +94,13 @@ def _declare(lib):
     lib.ossm_status_string.argtypes = [C.c_int]
     lib.ossm_sizeof_fwd_args.restype = C.c_size_t
     lib.ossm_sizeof_lion_args.restype = C.c_size_t
-    if lib.ossm_sizeof_fwd_args() != C.sizeof(FwdArgs) or lib.ossm_sizeof_lion_args() != C.sizeof(LionArgs):
+    lib.ossm_sizeof_ttt_args.restype = C.c_size_t
+    lib.ossm_ttt_workspace_bytes.restype = C.c_size_t
+    lib.ossm_ttt_workspace_bytes.argtypes = [C.POINTER(TttArgs)]
+    lib.ossm_ttt_wpred_step.restype = C.c_int
+    lib.ossm_ttt_wpred_step.argtypes = [C.POINTER(TttArgs), _vp, C.c_size_t, _vp]
+    if (lib.ossm_sizeof_fwd_args() != C.sizeof(FwdArgs) or lib.ossm_sizeof_lion_args() != C.sizeof(LionArgs)
+            or lib.ossm_sizeof_ttt_args() != C.sizeof(TttArgs)):
         raise RuntimeError("orthossm_b200: ctypes struct layout does not match the C ABI")
     return lib
 

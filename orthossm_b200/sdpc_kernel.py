@@ -331,6 +331,70 @@ def cheby_ema_forward_seqpar(x, coeffs, *, group=None, lambda_per_head=None, ema
     return out, final
 
 
+# ----------------------------------------------------------------------------
+# BASELINE-mode TTT: W_pred MSE objective + forget-gated Adam
+# ----------------------------------------------------------------------------
+
+def ttt_wpred_adam(x, coeffs, m, v, step, W_pred, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,
+                   gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None, chunk=2048,
+                   lr=1e-3, betas=(0.9, 0.999), eps=1e-8, spectral_pow=2.0, forget=True):
+    """Chunked forward + test-time training of the Chebyshev coefficients.
+
+    For each chunk of ``chunk`` tokens: the forward with the chunk-start
+    coefficients and the carried EMA state (fp32 states), the loss
+    mean_{t<L-1,d} (W_pred s_t - x_{t+1})^2 per sequence, its gradient through
+    the EMA, tanh and Chebyshev basis, scaled by 1/(k+1)^spectral_pow, and one
+    Adam step with the forget gate c <- lambda_h c - lr mhat/(sqrt(vhat)+eps).
+    The W_pred products run on cuBLAS (fp32); the adjoint, gradient and Adam
+    run in ``ossm_ttt_wpred_step``.
+
+    x: [B,S,D] (CUDA, bf16 or fp32); coeffs, m, v: [B,H,K,hd] (not modified);
+    step: Adam steps already taken.  Returns dict(out [B,S,D] fp32, coeffs, m,
+    v, step, final [B,D])."""
+    _need_cuda(x, coeffs, W_pred)
+    x = _rowmajor(x)
+    B, S, D = x.shape
+    dev = x.device
+    c = coeffs.detach().float().contiguous().clone()
+    m = m.detach().float().contiguous().clone()
+    v = v.detach().float().contiguous().clone()
+    H, K, hd = c.shape[1], c.shape[2], c.shape[3]
+    Wp = W_pred.to(dev, torch.float32).contiguous()
+    lam = torch.as_tensor(lambda_per_head if lambda_per_head is not None else [ema_momentum] * H,
+                          dtype=torch.float32, device=dev).contiguous()
+    state = None if init_state is None else init_state.to(dev, torch.float32).contiguous()
+    out = torch.empty(B, S, D, device=dev, dtype=torch.float32)
+    lib = L.lib()
+    stream = torch.cuda.current_stream(dev)
+    xdt = x.dtype if x.dtype in _DT else torch.float32
+    x = x.to(xdt)
+    for t0 in range(0, S, chunk):
+        Lc = min(chunk, S - t0)
+        xc = x[:, t0:t0 + Lc]
+        lt = None
+        if gate_weight is not None:
+            lt = gate_decay(xc, gate_weight, gate_bias, lam, gate_scale=gate_scale, gate_range=gate_range)
+        s, fin = cheby_ema_forward(xc, c, lambda_per_head=lam, lam_tok=lt, init_state=state,
+                                   out_dtype=torch.float32, out=out[:, t0:t0 + Lc])
+        gs = None
+        if Lc > 1:
+            r = torch.matmul(s[:, :-1], Wp.t()) - xc[:, 1:].float()
+            gs = torch.matmul(r, Wp).mul_(2.0 / ((Lc - 1) * D)).contiguous()
+        step += 1
+        a = L.TttArgs(B=B, L=Lc, H=H, head_dim=hd, degree=K, x=xc.data_ptr(), x_dtype=_DT[xdt],
+                      x_stride_b=xc.stride(0), x_stride_s=xc.stride(1), coeffs=c.data_ptr(), m=m.data_ptr(),
+                      v=v.data_ptr(), lam_h=lam.data_ptr(), momentum=float(ema_momentum), lam_tok=_ptr(lt),
+                      gs=_ptr(gs), lr=float(lr), beta1=float(betas[0]), beta2=float(betas[1]), eps=float(eps),
+                      spectral_pow=float(spectral_pow), step=int(step), forget=int(bool(forget)))
+        nbytes = lib.ossm_ttt_workspace_bytes(L.C.byref(a))
+        if nbytes == 0:
+            L.check(L.OSSM_EINVAL, "ttt_wpred_adam (argument check)")
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        L.check(lib.ossm_ttt_wpred_step(L.C.byref(a), ws.data_ptr(), nbytes, stream.cuda_stream), "ttt_wpred_step")
+        state = fin
+    return dict(out=out, coeffs=c, m=m, v=v, step=step, final=state)
+
+
 def gate_decay(x, gate_weight, gate_bias, lambda_per_head, *, gate_scale=0.008,
                gate_range=(0.0, 1.0), out=None):
     """Per-token decay of the dynamic-lambda gate, [B,S,H] float32:
