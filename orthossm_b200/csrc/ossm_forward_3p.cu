@@ -52,7 +52,7 @@ constexpr int kOffPart = kTile;                       // [8 warps][32 tokens][8]
 constexpr int kOffLam = kOffPart + kH * kL * kH * 4;  // [8 heads][32] float2 (l, 1 - l)
 constexpr int kOffBar = kOffLam + kH * kL * 8;
 constexpr int kAggSmem = kOffBar + 16 + 1024;        // + alignment slack
-constexpr int kSpans = 16;                           // carry kernel: warps per chain
+constexpr int kSpans = 32;                           // carry kernel: warps per chain
 
 struct Params {
   int B, S, K, nchunks;
@@ -86,14 +86,13 @@ OSSM_DEV float clamp4_nan(float v) {  // NaN-propagating clamp to [-4, 4]
   asm("max.NaN.f32 %0, %1, 0fC0800000;\n\tmin.NaN.f32 %0, %0, 0f40800000;" : "=f"(r) : "f"(v));
   return r;
 }
-// x / (1 + |x|) with x first clamped to +-2^60 (NaN passes through): one
-// flush-to-zero reciprocal, exact enough for every finite bf16 input, and
-// +-inf gives +-1 as the reference's 1 - 1/(1 + |x|) does.
+// sign(x) (1 - 1/(1 + |x|)), the reference's own form (sdpc_kernel.py:1078-1085)
+// with one flush-to-zero reciprocal: |x| = inf or beyond 2^126 gives +-1, NaN
+// stays NaN.  (The reference's 1e-7 floor on |x| moves xn by < 2e-7.)
 OSSM_DEV float softsign_fast(float x) {
-  float xc, r;
-  asm("max.NaN.f32 %0, %1, 0fDD800000;\n\tmin.NaN.f32 %0, %0, 0f5D800000;" : "=f"(xc) : "f"(x));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + fabsf(xc)));
-  return xc * r;
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + fabsf(x)));
+  return copysignf(1.0f - r, x);
 }
 
 // Chebyshev -> monomial coefficients with gamma folded in (T_0..T_7 written out).
