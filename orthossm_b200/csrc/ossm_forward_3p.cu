@@ -28,7 +28,7 @@
 // reference's semantics (u = 0 there).
 #include <cudaTypedefs.h>
 
-#include "ossm_sm100.cuh"
+#include "ossm_eval.cuh"
 
 // shared with the single-pass path (ossm_forward_tc.cu)
 namespace ossm {
@@ -41,11 +41,12 @@ bool encode_map(CUtensorMap* map, const void* base, int S, int B, long long ss, 
 namespace ossm {
 namespace p3 {
 
+using namespace ev;
+
 constexpr int kNT = 256;
 constexpr int kH = 8;    // heads (one warp each)
 constexpr int kHD = 64;  // channels per head
 constexpr int kD = kH * kHD;
-constexpr int kL = 32;               // tokens per chunk
 constexpr int kBox = kL * 128;       // one head's [32 x 128 B] box
 constexpr int kTile = kH * kBox;     // 32 KB
 constexpr int kOffPart = kTile;                       // [8 warps][32 tokens][8] f32
@@ -81,143 +82,6 @@ struct Params {
   const float* carry_in;  // [B][D] state entering the shard (or NULL: zero / init_state)
 };
 
-OSSM_DEV float clamp4_nan(float v) {  // NaN-propagating clamp to [-4, 4]
-  float r;
-  asm("max.NaN.f32 %0, %1, 0fC0800000;\n\tmin.NaN.f32 %0, %0, 0f40800000;" : "=f"(r) : "f"(v));
-  return r;
-}
-// sign(x) (1 - 1/(1 + |x|)), the reference's own form (sdpc_kernel.py:1078-1085)
-// with one flush-to-zero reciprocal: |x| = inf or beyond 2^126 gives +-1, NaN
-// stays NaN.  (The reference's 1e-7 floor on |x| moves xn by < 2e-7.)
-OSSM_DEV float softsign_fast(float x) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + fabsf(x)));
-  return copysignf(1.0f - r, x);
-}
-
-// Chebyshev -> monomial coefficients with gamma folded in (T_0..T_7 written out).
-OSSM_DEV void cheb_to_mono(const float2 (&ck)[8], float gamma, float2 (&a)[8]) {
-  const float2 g2 = make_float2(gamma, gamma);
-  auto w = [](float v) { return make_float2(v, v); };
-  a[0] = mul2(fma2(w(-1.f), ck[6], fma2(w(1.f), ck[4], fma2(w(-1.f), ck[2], ck[0]))), g2);
-  a[1] = mul2(fma2(w(-7.f), ck[7], fma2(w(5.f), ck[5], fma2(w(-3.f), ck[3], ck[1]))), g2);
-  a[2] = mul2(fma2(w(18.f), ck[6], fma2(w(-8.f), ck[4], mul2(w(2.f), ck[2]))), g2);
-  a[3] = mul2(fma2(w(56.f), ck[7], fma2(w(-20.f), ck[5], mul2(w(4.f), ck[3]))), g2);
-  a[4] = mul2(fma2(w(-48.f), ck[6], mul2(w(8.f), ck[4])), g2);
-  a[5] = mul2(fma2(w(-112.f), ck[7], mul2(w(16.f), ck[5])), g2);
-  a[6] = mul2(mul2(w(32.f), ck[6]), g2);
-  a[7] = mul2(mul2(w(64.f), ck[7]), g2);
-}
-
-// The lane's coefficients of (b, h): raw (precise) or gamma-folded monomial.
-template <bool PRECISE>
-OSSM_DEV void load_coeffs(const Params& p, int b, int h, int j0, float gamma, float (&c0)[8], float (&c1)[8]) {
-  const float* cb = p.coeffs + ((size_t)(b * kH + h) * p.K) * kHD + j0;
-  float2 ck[8], cf[8];
-#pragma unroll
-  for (int q = 0; q < 8; ++q)
-    ck[q] = q < p.K ? __ldg(reinterpret_cast<const float2*>(cb + q * kHD)) : make_float2(0.f, 0.f);
-  if (PRECISE) {
-#pragma unroll
-    for (int q = 0; q < 8; ++q) cf[q] = ck[q];
-  } else {
-    cheb_to_mono(ck, gamma, cf);
-  }
-#pragma unroll
-  for (int q = 0; q < 8; ++q) c0[q] = cf[q].x, c1[q] = cf[q].y;
-}
-
-// u = tanh(clamp(gamma y(xn), +-4)) for one channel of one token.
-// EXACT: the reference's semantics for every input (NaN -> u = 0,
-// sdpc_kernel.py:1164; +-inf -> xn = +-1, :1078-1085).  Otherwise a NaN input
-// comes out as NaN (caught per chunk); every other input takes the
-// reference's formula either way.
-template <bool PRECISE, bool EXACT>
-OSSM_DEV float eval_u1(float x, const float (&c)[8], float gamma) {
-  float xn;
-  if (PRECISE || EXACT) {
-    float xa, sg;
-    xn = softsign<PRECISE>(x, false, xa, sg);
-    if (!EXACT && x != x) xn = x;
-  } else {
-    xn = softsign_fast(x);
-  }
-  float y;
-  if (PRECISE) {  // Clenshaw on the raw coefficients, then gamma
-    const float x2 = 2.f * xn;
-    float u1 = c[7], u2 = 0.f;
-#pragma unroll
-    for (int q = 6; q >= 1; --q) {
-      const float tt = fmaf(x2, u1, c[q] - u2);
-      u2 = u1;
-      u1 = tt;
-    }
-    y = fmaf(xn, u1, c[0] - u2) * gamma;
-  } else {  // Horner on gamma-folded monomial coefficients
-    y = c[7];
-#pragma unroll
-    for (int q = 6; q >= 0; --q) y = fmaf(y, xn, c[q]);
-  }
-  if (EXACT) {
-    const float z = fminf(fmaxf(y, -4.f), 4.f);
-    return x != x ? 0.f : (PRECISE ? tanhf(z) : tanh_fast(z));
-  }
-  const float z = clamp4_nan(y);
-  return PRECISE ? tanhf(z) : tanh_fast(z);
-}
-template <bool PRECISE, bool EXACT>
-OSSM_DEV float2 eval_u(uint32_t raw, const float (&c0)[8], const float (&c1)[8], float gamma) {
-  return make_float2(eval_u1<PRECISE, EXACT>(__uint_as_float(raw << 16), c0, gamma),
-                     eval_u1<PRECISE, EXACT>(__uint_as_float(raw & 0xffff0000u), c1, gamma));
-}
-
-// s <- l s + (1 - l) u; token 0 of the sequence (first) folds the carried-in
-// state with the reference's clamp.
-OSSM_DEV float2 ema_step(float2 s, float2 lm, float2 u, bool first) {  // lm = (l, 1 - l)
-  if (first) return make_float2(clamp1(fmaf(lm.x, s.x, lm.y * u.x)), clamp1(fmaf(lm.x, s.y, lm.y * u.y)));
-  return fma2(make_float2(lm.x, lm.x), s, mul2(make_float2(lm.y, lm.y), u));
-}
-
-// The 32-token EMA of one chunk from state s (decays lam[0..31]); RAW(t) gives
-// the packed bf16 pair of token t, OUT(t, s) receives each state.
-template <bool PRECISE, bool EXACT, typename RawF, typename OutF>
-OSSM_DEV float2 ema_chunk(float2 s, const float2* lam, bool first, const float (&c0)[8], const float (&c1)[8],
-                          float gamma, RawF raw, OutF out) {
-#pragma unroll
-  for (int t = 0; t < kL; ++t) {
-    s = ema_step(s, lam[t], eval_u<PRECISE, EXACT>(raw(t), c0, c1, gamma), t == 0 && first);
-    out(t, s);
-  }
-  return s;
-}
-// The same with the reference's NaN / inf semantics as a rolled loop (the rare
-// recompute of a chunk that held such inputs).
-template <bool PRECISE, typename RawF, typename OutF>
-OSSM_DEV float2 ema_chunk_exact(float2 s, const float2* lam, bool first, const float (&c0)[8], const float (&c1)[8],
-                                float gamma, RawF raw, OutF out) {
-#pragma unroll 1
-  for (int t = 0; t < kL; ++t) {
-    s = ema_step(s, lam[t], eval_u<PRECISE, true>(raw(t), c0, c1, gamma), t == 0 && first);
-    out(t, s);
-  }
-  return s;
-}
-
-OSSM_DEV void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-OSSM_DEV void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-// byte offset of (token t, 16-byte chunk j) in a head's 128-byte-swizzled box
-OSSM_DEV uint32_t box_off(int t, int j) { return (uint32_t)(t * 128 + ((j ^ (t & 7)) << 4)); }
-
 // Decay of token (t0 + lane), head h, from a per-token input or the constant.
 OSSM_DEV float lam_token(const Params& p, const float* lam_tok, int b, int tg, int h, float lam_base) {
   if (tg >= p.S) return 1.f;  // past the end: the state is carried unchanged
@@ -250,7 +114,7 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
   }
   // while the tile lands: coefficients, gate weights, the caller's decay
   float c0[8], c1[8];
-  load_coeffs<PRECISE>(p, b, h, j0, gamma, c0, c1);
+  load_coeffs<PRECISE>(p.coeffs, p.K, b, h, j0, gamma, c0, c1);
   const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
   float lam = GATE ? lam_base : lam_token(p, p.lam_in, b, tg, h, lam_base);
   uint32_t whi[4][2], wlo[4][2];  // mma B fragments of W[gid][h*64 + ks*16 + ...], split bf16 hi + lo
@@ -467,7 +331,7 @@ __global__ void __launch_bounds__(kNT, 3) p3_out_kernel(const Params p, const fl
   const float lam = lam_token(p, lam_tok, b, t0 + lane, h, lam_base);
   lam_s[h * kL + lane] = make_float2(lam, 1.f - lam);
   float c0[8], c1[8];
-  load_coeffs<PRECISE>(p, b, h, j0, gamma, c0, c1);
+  load_coeffs<PRECISE>(p.coeffs, p.K, b, h, j0, gamma, c0, c1);
   __syncwarp();
 
   const __nv_bfloat16* xp = p.x + (size_t)b * p.xsb + (size_t)t0 * p.xss + ch0;
