@@ -188,6 +188,41 @@ typedef struct {
 int ossm_cheby_rkv_lion(const ossm_lion_args* a, ossm_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Backward of ossm_cheby_ema_fwd (Clenshaw evaluation, fused semantics):
+ * given grad_out = dL/dout [B,S,D], writes grad_x [B,S,D], grad_coeffs
+ * [B,H,degree,head_dim] and (if not NULL) grad_init [B,D].  The decays (lam_h /
+ * momentum, or the per-token lam_tok a gated forward used) are constants, as
+ * in the reference's backward (FusedChebyRKVv10.backward,
+ * sdpc_kernel.py:2435-2515, gradients for x and the coefficients only):
+ *   adj_t = g_t + a_{t+1} adj_{t+1};  dy_t = (1-a_t) adj_t (1-u_t^2) gamma_h [|z_t| < 4];
+ *   dc_k = sum_t dy_t T_k(xn_t);  dx_t = dy_t y'(xn_t) / (1+|x_t|)^2;
+ *   d init = a_0 adj_0 (zero where the token-0 clamp bites).
+ * head_dim <= 64.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  int32_t B, S, H, head_dim, degree;
+  const void* x;                     /* the forward's input */
+  int32_t x_dtype;
+  int64_t x_stride_b, x_stride_s;
+  const float* coeffs;               /* [B,H,degree,head_dim] */
+  const float* lam_h;                /* [H] or NULL (momentum) */
+  float momentum;
+  const float* lam_tok;              /* [B,S,H] or NULL */
+  const float* init_state;           /* [B,D] or NULL: the forward's carried-in state */
+  const void* grad_out;              /* dL/dout */
+  int32_t grad_out_dtype;
+  int64_t grad_out_stride_b, grad_out_stride_s;
+  void* grad_x;                      /* dL/dx (written) */
+  int32_t grad_x_dtype;
+  int64_t grad_x_stride_b, grad_x_stride_s;
+  float* grad_coeffs;                /* dL/dcoeffs (written) */
+  float* grad_init;                  /* dL/dinit_state [B,D] (written) or NULL */
+} ossm_bwd_args;
+
+size_t ossm_bwd_workspace_bytes(const ossm_bwd_args* a);
+int ossm_cheby_ema_bwd(const ossm_bwd_args* a, void* workspace, size_t workspace_bytes, ossm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * BASELINE-mode TTT step for one chunk (no
  * counterpart kernel in the reference, whose TTT is the local gated-error Lion
  * step of sdpc_kernel.py:2126-2287).  Inputs: the chunk's x, its coefficients
@@ -226,6 +261,7 @@ const char* ossm_status_string(int status);
 size_t ossm_sizeof_fwd_args(void);
 size_t ossm_sizeof_lion_args(void);
 size_t ossm_sizeof_ttt_args(void);
+size_t ossm_sizeof_bwd_args(void);
 
 #ifdef __cplusplus
 }

@@ -25,7 +25,8 @@ EXPORTED = (
     "ossm_workspace_status", "ossm_fwd_shard_aggregate", "ossm_fwd_shard_output",
     "ossm_cheby_rkv_lion", "ossm_version", "ossm_status_string",
     "ossm_sizeof_fwd_args", "ossm_sizeof_lion_args", "ossm_sizeof_ttt_args",
-    "ossm_ttt_workspace_bytes", "ossm_ttt_wpred_step",
+    "ossm_ttt_workspace_bytes", "ossm_ttt_wpred_step", "ossm_sizeof_bwd_args", "ossm_bwd_workspace_bytes",
+    "ossm_cheby_ema_bwd",
 )
 
 _vp = C.c_void_p
@@ -68,6 +69,17 @@ class TttArgs(C.Structure):
     ]
 
 
+class BwdArgs(C.Structure):
+    _fields_ = [
+        ("B", _i32), ("S", _i32), ("H", _i32), ("head_dim", _i32), ("degree", _i32),
+        ("x", _vp), ("x_dtype", _i32), ("x_stride_b", _i64), ("x_stride_s", _i64),
+        ("coeffs", _vp), ("lam_h", _vp), ("momentum", _f32), ("lam_tok", _vp), ("init_state", _vp),
+        ("grad_out", _vp), ("grad_out_dtype", _i32), ("grad_out_stride_b", _i64), ("grad_out_stride_s", _i64),
+        ("grad_x", _vp), ("grad_x_dtype", _i32), ("grad_x_stride_b", _i64), ("grad_x_stride_s", _i64),
+        ("grad_coeffs", _vp), ("grad_init", _vp),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -95,12 +107,17 @@ def _declare(lib):
     lib.ossm_sizeof_fwd_args.restype = C.c_size_t
     lib.ossm_sizeof_lion_args.restype = C.c_size_t
     lib.ossm_sizeof_ttt_args.restype = C.c_size_t
+    lib.ossm_sizeof_bwd_args.restype = C.c_size_t
+    lib.ossm_bwd_workspace_bytes.restype = C.c_size_t
+    lib.ossm_bwd_workspace_bytes.argtypes = [C.POINTER(BwdArgs)]
+    lib.ossm_cheby_ema_bwd.restype = C.c_int
+    lib.ossm_cheby_ema_bwd.argtypes = [C.POINTER(BwdArgs), _vp, C.c_size_t, _vp]
     lib.ossm_ttt_workspace_bytes.restype = C.c_size_t
     lib.ossm_ttt_workspace_bytes.argtypes = [C.POINTER(TttArgs)]
     lib.ossm_ttt_wpred_step.restype = C.c_int
     lib.ossm_ttt_wpred_step.argtypes = [C.POINTER(TttArgs), _vp, C.c_size_t, _vp]
     if (lib.ossm_sizeof_fwd_args() != C.sizeof(FwdArgs) or lib.ossm_sizeof_lion_args() != C.sizeof(LionArgs)
-            or lib.ossm_sizeof_ttt_args() != C.sizeof(TttArgs)):
+            or lib.ossm_sizeof_ttt_args() != C.sizeof(TttArgs) or lib.ossm_sizeof_bwd_args() != C.sizeof(BwdArgs)):
         raise RuntimeError("orthossm_b200: ctypes struct layout does not match the C ABI")
     return lib
 

@@ -219,6 +219,82 @@ def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate
                       out_dtype=None, return_tanh=False, eval_mode="clenshaw",
                       fast_path_semantics=False, precise=None, out=None, final_state=None,
                       lam_tok=None, force_generic=False):
+    """Fused softsign -> degree-K Chebyshev -> gamma_h -> tanh -> lambda-EMA,
+    differentiable in ``x``, ``coeffs`` and ``init_state`` when autograd needs
+    it (``ossm_cheby_ema_bwd``; the decays are constants, as in the
+    reference's backward).  See ``_cheby_ema_forward`` for the arguments."""
+    needs_grad = torch.is_grad_enabled() and any(
+        t is not None and isinstance(t, torch.Tensor) and t.requires_grad for t in (x, coeffs, init_state))
+    if not needs_grad:
+        return _cheby_ema_forward(
+            x, coeffs, lambda_per_head=lambda_per_head, ema_momentum=ema_momentum, gate_weight=gate_weight,
+            gate_bias=gate_bias, gate_scale=gate_scale, gate_range=gate_range, init_state=init_state,
+            out_dtype=out_dtype, return_tanh=return_tanh, eval_mode=eval_mode,
+            fast_path_semantics=fast_path_semantics, precise=precise, out=out, final_state=final_state,
+            lam_tok=lam_tok, force_generic=force_generic)
+    if eval_mode != "clenshaw" or fast_path_semantics or return_tanh or out is not None or final_state is not None:
+        raise NotImplementedError("orthossm_b200: the backward covers the Clenshaw forward with fresh outputs")
+    H = coeffs.shape[1]
+    lam = torch.as_tensor(lambda_per_head if lambda_per_head is not None else [ema_momentum] * H,
+                          dtype=torch.float32, device=x.device).contiguous()
+    if lam_tok is None and gate_weight is not None:  # the gate's decays, held constant
+        lam_tok = gate_decay(x.detach(), gate_weight.detach(), gate_bias.detach(), lam, gate_scale=gate_scale,
+                             gate_range=gate_range)
+    opts = dict(ema_momentum=float(ema_momentum), out_dtype=out_dtype, precise=precise,
+                force_generic=force_generic)
+    return _ChebyEmaFn.apply(x, coeffs, init_state, lam, lam_tok, opts)
+
+
+class _ChebyEmaFn(torch.autograd.Function):
+    """Autograd node of the forward; backward through ``ossm_cheby_ema_bwd``."""
+
+    @staticmethod
+    def forward(ctx, x, coeffs, init_state, lam, lam_tok, opts):
+        out, fin = _cheby_ema_forward(x.detach(), coeffs.detach(), lambda_per_head=lam, lam_tok=lam_tok,
+                                      init_state=None if init_state is None else init_state.detach(), **opts)
+        ctx.save_for_backward(x, coeffs, init_state, lam, lam_tok)
+        ctx.has_init = init_state is not None
+        ctx.momentum = opts["ema_momentum"]
+        return out, fin
+
+    @staticmethod
+    def backward(ctx, g_out, g_fin):
+        x, coeffs, init_state, lam, lam_tok = ctx.saved_tensors
+        x = _rowmajor(x.detach())
+        if x.dtype not in _DT:
+            x = x.float()
+        B, S, D = x.shape
+        c = coeffs.detach().contiguous().float()
+        H, K, hd = c.shape[1], c.shape[2], c.shape[3]
+        g = (torch.zeros(B, S, D, device=x.device) if g_out is None else g_out.float()).contiguous()
+        if g_fin is not None:  # the final state is the last token's state
+            g = g.clone()
+            g[:, -1] += g_fin.float()
+        gx = torch.empty(B, S, D, device=x.device, dtype=torch.float32)
+        gc = torch.empty_like(c)
+        gi = torch.empty(B, D, device=x.device) if ctx.has_init else None
+        init = None if init_state is None else init_state.detach().float().contiguous()
+        a = L.BwdArgs(B=B, S=S, H=H, head_dim=hd, degree=K, x=x.data_ptr(), x_dtype=_DT[x.dtype],
+                      x_stride_b=x.stride(0), x_stride_s=x.stride(1), coeffs=c.data_ptr(), lam_h=lam.data_ptr(),
+                      momentum=ctx.momentum, lam_tok=_ptr(lam_tok), init_state=_ptr(init), grad_out=g.data_ptr(),
+                      grad_out_dtype=L.OSSM_F32, grad_out_stride_b=g.stride(0), grad_out_stride_s=g.stride(1),
+                      grad_x=gx.data_ptr(), grad_x_dtype=L.OSSM_F32, grad_x_stride_b=gx.stride(0),
+                      grad_x_stride_s=gx.stride(1), grad_coeffs=gc.data_ptr(), grad_init=_ptr(gi))
+        lib = L.lib()
+        nbytes = lib.ossm_bwd_workspace_bytes(L.C.byref(a))
+        if nbytes == 0:
+            L.check(L.OSSM_EINVAL, "cheby_ema_forward backward (argument check)")
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+        L.check(lib.ossm_cheby_ema_bwd(L.C.byref(a), ws.data_ptr(), nbytes,
+                                       torch.cuda.current_stream(x.device).cuda_stream), "cheby_ema_bwd")
+        return gx.to(ctx.saved_tensors[0].dtype), gc.to(coeffs.dtype), gi, None, None, None
+
+
+def _cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,
+                       gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None,
+                       out_dtype=None, return_tanh=False, eval_mode="clenshaw",
+                       fast_path_semantics=False, precise=None, out=None, final_state=None,
+                       lam_tok=None, force_generic=False):
     """Fused softsign -> degree-K Chebyshev -> gamma_h -> tanh -> lambda-EMA.
 
     x: [B,S,D] float32 or bfloat16 (CUDA); coeffs: [B,H,K,hd] float32.
