@@ -183,6 +183,8 @@ typedef struct {
   float* tanh_out;                /* optional f32 [B,S,D] (contiguous strides of out) */
   float* final_state;             /* optional [B,D]: EMA state at the end of the last chunk */
   uint32_t flags;                 /* OSSM_EVAL_* */
+  float* coeff_trace;             /* optional [ceil(S/chunk)][B,H,degree,head_dim]: the
+                                     coefficients each chunk starts from (for the backward) */
 } ossm_lion_args;
 
 int ossm_cheby_rkv_lion(const ossm_lion_args* a, ossm_stream_t stream);
@@ -197,7 +199,7 @@ int ossm_cheby_rkv_lion(const ossm_lion_args* a, ossm_stream_t stream);
  *   adj_t = g_t + a_{t+1} adj_{t+1};  dy_t = (1-a_t) adj_t (1-u_t^2) gamma_h [|z_t| < 4];
  *   dc_k = sum_t dy_t T_k(xn_t);  dx_t = dy_t y'(xn_t) / (1+|x_t|)^2;
  *   d init = a_0 adj_0 (zero where the token-0 clamp bites).
- * head_dim <= 64.
+ * head_dim <= 256.
  * ------------------------------------------------------------------------ */
 typedef struct {
   int32_t B, S, H, head_dim, degree;
@@ -217,6 +219,12 @@ typedef struct {
   int64_t grad_x_stride_b, grad_x_stride_s;
   float* grad_coeffs;                /* dL/dcoeffs (written) */
   float* grad_init;                  /* dL/dinit_state [B,D] (written) or NULL */
+  int32_t segment;                   /* 0, or the forward restarted its EMA from zero every
+                                        `segment` tokens (the reference's chunk loop) */
+  const float* segment_coeffs;       /* with segment: [ceil(S/segment)][B,H,degree,head_dim], the
+                                        coefficients of each segment (coeffs is then segment 0's) */
+  uint32_t flags;                    /* OSSM_F_FASTPATH: the fast-path forward (unclamped tanh,
+                                        sign(0) = 0, NaN -> xn = 0) */
 } ossm_bwd_args;
 
 size_t ossm_bwd_workspace_bytes(const ossm_bwd_args* a);
@@ -235,7 +243,7 @@ int ossm_cheby_ema_bwd(const ossm_bwd_args* a, void* workspace, size_t workspace
  * forget == 0), with bias corrections for Adam step `step` (>= 1).
  * ------------------------------------------------------------------------ */
 typedef struct {
-  int32_t B, L, H, head_dim, degree; /* head_dim <= 64, degree <= 8 */
+  int32_t B, L, H, head_dim, degree; /* head_dim <= 256, degree <= 8 */
   const void* x;                     /* [B,L,H*head_dim] */
   int32_t x_dtype;
   int64_t x_stride_b, x_stride_s;

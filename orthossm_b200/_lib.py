@@ -55,7 +55,7 @@ class LionArgs(C.Structure):
         ("ema_momentum", _f32), ("base_lr", _f32), ("beta1", _f32), ("beta2", _f32),
         ("weight_decay", _f32),
         ("lut", _vp), ("out", _vp), ("out_dtype", _i32), ("out_stride_b", _i64), ("out_stride_s", _i64),
-        ("tanh_out", _vp), ("final_state", _vp), ("flags", C.c_uint32),
+        ("tanh_out", _vp), ("final_state", _vp), ("flags", C.c_uint32), ("coeff_trace", _vp),
     ]
 
 
@@ -76,7 +76,8 @@ class BwdArgs(C.Structure):
         ("coeffs", _vp), ("lam_h", _vp), ("momentum", _f32), ("lam_tok", _vp), ("init_state", _vp),
         ("grad_out", _vp), ("grad_out_dtype", _i32), ("grad_out_stride_b", _i64), ("grad_out_stride_s", _i64),
         ("grad_x", _vp), ("grad_x_dtype", _i32), ("grad_x_stride_b", _i64), ("grad_x_stride_s", _i64),
-        ("grad_coeffs", _vp), ("grad_init", _vp),
+        ("grad_coeffs", _vp), ("grad_init", _vp), ("segment", _i32), ("segment_coeffs", _vp),
+        ("flags", C.c_uint32),
     ]
 
 

@@ -45,6 +45,7 @@ struct LionParams {
   long long osb, oss;
   float* tanh_out;
   float* fin;
+  float* trace;  // optional [nchunks][B,H,K,HD]: the coefficients each chunk starts from
   uint32_t flags;
 };
 
@@ -155,6 +156,12 @@ __global__ void __launch_bounds__(lion::kNT, 1) lion_kernel(const LionParams p) 
 #pragma unroll
       for (int k = 0; k < 8; ++k) g[q][k] = 0.f;
     if (tid < G) carry_s[tid] = 0.f;  // EMA reset per chunk (:2398)
+    if (p.trace && tid < 8 * G) {  // the chunk's starting coefficients, for the backward
+      const int k = tid / G, jj = tid % G;
+      if (k < p.K)
+        p.trace[(size_t)(cs / p.chunk) * ((size_t)p.B * p.H * p.K * p.HD) + cbase + (size_t)k * p.HD + jj] =
+            csm[k * G + jj];
+    }
     __syncthreads();
 
     for (int ps = cs; ps < ce; ps += p.Lp) {
@@ -365,6 +372,7 @@ extern "C" int ossm_cheby_rkv_lion(const ossm_lion_args* a, ossm_stream_t stream
   p.tanh_out = a->tanh_out;
   p.fin = a->final_state;
   p.flags = a->flags;
+  p.trace = a->coeff_trace;
   const long long grid = (long long)a->B * a->H * p.ngroups;
   if (grid > 0x7fffffffLL) return OSSM_EINVAL;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

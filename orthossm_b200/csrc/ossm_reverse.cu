@@ -12,7 +12,11 @@
 //   dL/dc_k = sum_t dy_t T_k(xn_t)
 //   dL/dx_t = dy_t y'(xn_t) / (1 + |x_t|)^2            (y' = sum_k c_k T_k')
 //   dL/ds_{-1} = a_0 adj_0                               (the carried-in state)
-// with the token-0 clamp passing no gradient where it bites.  The decays are
+// with the token-0 clamp passing no gradient where it bites.  A segmented
+// backward (the reference's chunk loop: the EMA restarts from zero every
+// `segment` tokens, each chunk with its own coefficients) cuts the adjoint at
+// every restart and returns the gradient of segment 0's coefficients; the
+// fast-path backward drops the tanh clamp and uses x.sign().  The decays are
 // constants (no gradient through the gate), as in the reference's backward
 // (FusedChebyRKVv10.backward, sdpc_kernel.py:2435-2515, which returns
 // gradients for x and the coefficients only).
@@ -44,7 +48,7 @@ constexpr int kL = 32;  // tokens per sub-chunk
 constexpr int kMaxK = 8;
 
 struct Params {
-  int B, L, H, HD, K, nq;
+  int B, L, H, HD, K, nq, ngrp;  // ngrp: 64-channel groups per head (one warp each)
   const void* x;
   int x_bf16;
   long long xsb, xss;
@@ -65,6 +69,9 @@ struct Params {
   float* gc;           // [B,H,K,HD]
   float* ginit;        // [B,D] or NULL
   const float* init;   // [B,D] or NULL (for the token-0 clamp)
+  int seg;             // backward: the forward restarted its EMA every seg tokens (0: never)
+  const float* cseg;   // [nseg][B,H,K,HD] coefficients per segment (NULL: coeffs)
+  int fastpath;        // backward of the fast-path forward: unclamped tanh, sign(0) = 0
   // TTT optimizer
   float* m;
   float* v;
@@ -88,6 +95,15 @@ OSSM_DEV float decay(const Params& p, int b, int t, int h) {  // 1 past the end:
   if (p.lam_tok) return __ldg(p.lam_tok + ((size_t)b * p.L + t) * p.H + h);
   return p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
 }
+// the decay that carries the adjoint from token t+1 back to token t: zero
+// across a restart of the forward's EMA
+OSSM_DEV float carry_decay(const Params& p, int b, int t1, int h) {
+  if (p.seg > 0 && t1 % p.seg == 0) return 0.f;
+  return decay(p, b, t1, h);
+}
+OSSM_DEV const float* coeffs_at(const Params& p, int t) {
+  return (p.seg > 0 && p.cseg) ? p.cseg + (size_t)(t / p.seg) * ((size_t)p.B * p.H * p.K * p.HD) : p.coeffs;
+}
 OSSM_DEV float gval(const Params& p, int b, int t, int ch) {
   if (p.ttt) {
     const int D = p.H * p.HD;
@@ -96,41 +112,44 @@ OSSM_DEV float gval(const Params& p, int b, int t, int ch) {
   return ld_any(p.g, p.g_bf16, (size_t)b * p.gsb + (size_t)t * p.gss + ch);
 }
 
-// Lane covers channels lane and lane + 32 of the head (head_dim <= 64).
+// A warp covers one 64-channel group of a head; lane = channels
+// grp*64 + lane and grp*64 + lane + 32.
 __global__ void __launch_bounds__(256) rev_agg_kernel(const Params p) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= p.B * p.H * p.nq) return;
-  const int q = warp % p.nq, bh = warp / p.nq, b = bh / p.H, h = bh % p.H;
+  if (warp >= p.B * p.H * p.ngrp * p.nq) return;
+  const int q = warp % p.nq, grp = (warp / p.nq) % p.ngrp, bh = warp / (p.nq * p.ngrp), b = bh / p.H, h = bh % p.H;
+  const int jb = grp * 64 + lane;
   const int t0 = q * kL;
   float R[2] = {0.f, 0.f};
   float A = 1.f;
   for (int t = min(t0 + kL, p.L) - 1; t >= t0; --t) {
-    const float an = decay(p, b, t + 1, h);  // a_{t+1}
+    const float an = carry_decay(p, b, t + 1, h);  // a_{t+1}
     A *= an;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const int j = lane + 32 * e;
+      const int j = jb + 32 * e;
       if (j < p.HD) R[e] = fmaf(an, R[e], gval(p, b, t, h * p.HD + j));
     }
   }
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
-    const int j = lane + 32 * e;
+    const int j = jb + 32 * e;
     if (j < p.HD) p.Rq[((size_t)bh * p.nq + q) * p.HD + j] = R[e];
   }
-  if (lane == 0) p.Aq[(size_t)bh * p.nq + q] = A;
+  if (lane == 0 && grp == 0) p.Aq[(size_t)bh * p.nq + q] = A;
 }
 
 // C_q = R_q + A_q C_{q+1}, C_nq = 0: the adjoint at sub-chunk q's first token;
 // Cq[q] keeps C_{q+1}, the adjoint entering sub-chunk q from the right.
 __global__ void __launch_bounds__(32) rev_carry_kernel(const Params p) {
-  const int bh = blockIdx.x, lane = threadIdx.x;
+  const int bh = blockIdx.x / p.ngrp, lane = threadIdx.x;
+  const int jb = (blockIdx.x % p.ngrp) * 64 + lane;
   float C[2] = {0.f, 0.f};
   for (int q = p.nq - 1; q >= 0; --q) {
     const float A = p.Aq[(size_t)bh * p.nq + q];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const int j = lane + 32 * e;
+      const int j = jb + 32 * e;
       if (j < p.HD) {
         p.Cq[((size_t)bh * p.nq + q) * p.HD + j] = C[e];
         C[e] = fmaf(A, C[e], p.Rq[((size_t)bh * p.nq + q) * p.HD + j]);
@@ -141,37 +160,55 @@ __global__ void __launch_bounds__(32) rev_carry_kernel(const Params p) {
 
 __global__ void __launch_bounds__(256) rev_grad_kernel(const Params p) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= p.B * p.H * p.nq) return;
-  const int q = warp % p.nq, bh = warp / p.nq, b = bh / p.H, h = bh % p.H;
+  if (warp >= p.B * p.H * p.ngrp * p.nq) return;
+  const int q = warp % p.nq, grp = (warp / p.nq) % p.ngrp, bh = warp / (p.nq * p.ngrp), b = bh / p.H, h = bh % p.H;
+  const int jb = grp * 64 + lane;
   const int t0 = q * kL, t1 = min(t0 + kL, p.L);
   const int D = p.H * p.HD;
   const float gamma = 0.98f - 0.06f * (float)h / (float)p.H;
   float acc[2][kMaxK];
   float cf[2][kMaxK];
   float adj[2];
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const int j = lane + 32 * e;
-    adj[e] = j < p.HD ? p.Cq[((size_t)bh * p.nq + q) * p.HD + j] : 0.f;
-#pragma unroll
-    for (int k = 0; k < kMaxK; ++k) {
-      acc[e][k] = 0.f;
-      cf[e][k] = (j < p.HD && k < p.K) ? p.coeffs[(((size_t)b * p.H + h) * p.K + k) * p.HD + j] : 0.f;
-    }
-  }
-  for (int t = t1 - 1; t >= t0; --t) {
-    const float an = decay(p, b, t + 1, h), at = decay(p, b, t, h);
+  int cur_seg = -1;
+  // the coefficients the forward used at token t (one set, or one per segment)
+  auto load_cf = [&](int t) {
+    const float* cb = coeffs_at(p, t);
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const int j = lane + 32 * e;
+      const int j = jb + 32 * e;
+#pragma unroll
+      for (int k = 0; k < kMaxK; ++k)
+        cf[e][k] = (j < p.HD && k < p.K) ? cb[(((size_t)b * p.H + h) * p.K + k) * p.HD + j] : 0.f;
+    }
+  };
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int j = jb + 32 * e;
+    adj[e] = j < p.HD ? p.Cq[((size_t)bh * p.nq + q) * p.HD + j] : 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxK; ++k) acc[e][k] = 0.f;
+  }
+  for (int t = t1 - 1; t >= t0; --t) {
+    const int sg_t = p.seg > 0 ? t / p.seg : 0;
+    if (sg_t != cur_seg) {
+      cur_seg = sg_t;
+      load_cf(t);
+    }
+    const float an = carry_decay(p, b, t + 1, h), at = decay(p, b, t, h);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int j = jb + 32 * e;
       if (j >= p.HD) continue;
       const int ch = h * p.HD + j;
       adj[e] = fmaf(an, adj[e], gval(p, b, t, ch));
       const float x = xval(p, b, t, ch);
+      const bool nan = x != x;
       float dx = 0.f;
-      if (x == x) {  // a NaN input has u = 0 and passes no gradient
+      // a NaN input: u = 0 in the fused forward (no gradient at all); xn = 0 in the fast path
+      if (!nan || p.fastpath) {
         float xa, sg;
-        const float xn = softsign<true>(x, false, xa, sg);
+        // fused: sign(0) = +1; fast path: x.sign() (0 at 0) and NaN -> 0
+        const float xn = nan ? 0.f : (p.fastpath && x == 0.f ? 0.f : softsign<true>(x, false, xa, sg));
         // T_k(xn), T_k'(xn); y = sum c_k T_k, y' = sum c_k T_k'
         float T[kMaxK], dT[kMaxK];
         T[0] = 1.f;
@@ -190,27 +227,23 @@ __global__ void __launch_bounds__(256) rev_grad_kernel(const Params p) {
           yp = fmaf(cf[e][k], dT[k], yp);
         }
         const float z = gamma * y;
-        if (fabsf(z) < 4.f) {  // the clamp passes no gradient where it bites
-          const float u = tanhf(z);
-          float w = 1.f - at;  // ds_t / du_t
-          if (!p.ttt && t == 0) {  // token 0: the carried-in state and the clamp
-            const float iv = p.init ? p.init[(size_t)b * D + ch] : 0.f;
-            const float pre = fmaf(at, iv, (1.f - at) * u);
-            const bool pass = fabsf(pre) <= 1.f;
-            if (!pass) w = 0.f;
-            if (p.ginit) p.ginit[(size_t)b * D + ch] = pass ? at * adj[e] : 0.f;
-          }
-          const float dy = w * adj[e] * (1.f - u * u) * gamma;
+        const bool live = p.fastpath || fabsf(z) < 4.f;  // the fused clamp passes no gradient where it bites
+        const float u = p.fastpath ? tanhf(z) : tanhf(fminf(fmaxf(z, -4.f), 4.f));
+        float w = 1.f - at;  // ds_t / du_t
+        if (!p.ttt && t == 0 && !p.fastpath) {  // token 0: the carried-in state and its clamp
+          const float iv = p.init ? p.init[(size_t)b * D + ch] : 0.f;
+          const bool pass = fabsf(fmaf(at, iv, (1.f - at) * u)) <= 1.f;
+          if (!pass) w = 0.f;
+          if (p.ginit) p.ginit[(size_t)b * D + ch] = pass ? at * adj[e] : 0.f;
+        }
+        const float dy = live ? w * adj[e] * (1.f - u * u) * gamma : 0.f;
+        if (p.seg == 0 || t < p.seg)  // segmented: the gradient of segment 0's coefficients
 #pragma unroll
           for (int k = 0; k < kMaxK; ++k) acc[e][k] = fmaf(dy, T[k], acc[e][k]);
-          const float d1 = 1.f + fabsf(x);
-          dx = dy * yp / (d1 * d1);
-        } else if (!p.ttt && t == 0 && p.ginit) {  // u saturated: only the state's path remains
-          const float iv = p.init ? p.init[(size_t)b * D + ch] : 0.f;
-          const float u = tanhf(fminf(fmaxf(z, -4.f), 4.f));
-          p.ginit[(size_t)b * D + ch] = fabsf(fmaf(at, iv, (1.f - at) * u)) <= 1.f ? at * adj[e] : 0.f;
-        }
-      } else if (!p.ttt && t == 0 && p.ginit) {
+        const float d1 = 1.f + fabsf(x);
+        // dxn/dx = 1/(1+|x|)^2 (the fast path's clamp of |x| at 1e-7 passes nothing below it)
+        if (!nan && !(p.fastpath && fabsf(x) < 1e-7f)) dx = dy * yp / (d1 * d1);
+      } else if (!p.ttt && t == 0 && p.ginit) {  // fused, NaN at token 0: u = 0
         const float iv = p.init ? p.init[(size_t)b * D + ch] : 0.f;
         p.ginit[(size_t)b * D + ch] = fabsf(at * iv) <= 1.f ? at * adj[e] : 0.f;
       }
@@ -225,7 +258,7 @@ __global__ void __launch_bounds__(256) rev_grad_kernel(const Params p) {
   }
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
-    const int j = lane + 32 * e;
+    const int j = jb + 32 * e;
     if (j >= p.HD) continue;
 #pragma unroll
     for (int k = 0; k < kMaxK; ++k)
@@ -272,10 +305,10 @@ int run(Params& p, char* ws, cudaStream_t st) {
   p.Aq = reinterpret_cast<float*>(ws + off);
   off += al256(BH * p.nq * 4);
   p.part = reinterpret_cast<float*>(ws + off);
-  const size_t warps = BH * p.nq;
+  const size_t warps = BH * p.ngrp * p.nq;
   const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
   rev_agg_kernel<<<blocks, 256, 0, st>>>(p);
-  rev_carry_kernel<<<(unsigned)BH, 32, 0, st>>>(p);
+  rev_carry_kernel<<<(unsigned)(BH * p.ngrp), 32, 0, st>>>(p);
   rev_grad_kernel<<<blocks, 256, 0, st>>>(p);
   const size_t per = BH * p.K * p.HD;
   rev_reduce_kernel<<<(unsigned)((per + 255) / 256), 256, 0, st>>>(p);
@@ -290,6 +323,7 @@ void common(Params& p, int B, int L, int H, int HD, int K, const void* x, int x_
   p.HD = HD;
   p.K = K;
   p.nq = (L + kL - 1) / kL;
+  p.ngrp = (HD + 63) / 64;
   p.x = x;
   p.x_bf16 = x_dtype == OSSM_BF16;
   p.xsb = xsb;
@@ -307,6 +341,9 @@ void common(Params& p, int B, int L, int H, int HD, int K, const void* x, int x_
   p.gc = nullptr;
   p.ginit = nullptr;
   p.init = nullptr;
+  p.seg = 0;
+  p.cseg = nullptr;
+  p.fastpath = 0;
   p.m = p.v = nullptr;
   p.lr = p.beta1 = p.beta2 = p.eps = p.spow = 0.f;
   p.bc1 = p.bc2 = 1.f;
@@ -320,7 +357,7 @@ using namespace ossm;
 
 namespace {
 int ttt_validate(const ossm_ttt_args* a) {
-  if (!a || a->B < 1 || a->L < 1 || a->H < 1 || a->head_dim < 1 || a->head_dim > 64 || a->degree < 1 ||
+  if (!a || a->B < 1 || a->L < 1 || a->H < 1 || a->head_dim < 1 || a->head_dim > 256 || a->degree < 1 ||
       a->degree > rev::kMaxK)
     return OSSM_EINVAL;
   if (!a->x || !a->coeffs || !a->m || !a->v || (a->L > 1 && !a->gs)) return OSSM_EINVAL;
@@ -329,10 +366,11 @@ int ttt_validate(const ossm_ttt_args* a) {
   return OSSM_OK;
 }
 int bwd_validate(const ossm_bwd_args* a) {
-  if (!a || a->B < 1 || a->S < 1 || a->H < 1 || a->head_dim < 1 || a->head_dim > 64 || a->degree < 1 ||
+  if (!a || a->B < 1 || a->S < 1 || a->H < 1 || a->head_dim < 1 || a->head_dim > 256 || a->degree < 1 ||
       a->degree > rev::kMaxK)
     return OSSM_EINVAL;
   if (!a->x || !a->coeffs || !a->grad_out || !a->grad_x || !a->grad_coeffs) return OSSM_EINVAL;
+  if (a->segment < 0 || (a->segment > 0 && a->segment < a->S && !a->segment_coeffs)) return OSSM_EINVAL;
   for (int dt : {a->x_dtype, a->grad_out_dtype, a->grad_x_dtype})
     if (dt != OSSM_F32 && dt != OSSM_BF16) return OSSM_EINVAL;
   return OSSM_OK;
@@ -394,5 +432,8 @@ extern "C" int ossm_cheby_ema_bwd(const ossm_bwd_args* a, void* workspace, size_
   p.gc = a->grad_coeffs;
   p.ginit = a->grad_init;
   p.init = a->init_state;
+  p.seg = a->segment > 0 && a->segment < a->S ? a->segment : 0;
+  p.cseg = p.seg ? a->segment_coeffs : nullptr;
+  p.fastpath = (a->flags & OSSM_F_FASTPATH) ? 1 : 0;
   return rev::run(p, static_cast<char*>(workspace), reinterpret_cast<cudaStream_t>(stream));
 }

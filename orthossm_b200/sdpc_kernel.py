@@ -232,7 +232,7 @@ def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate
             out_dtype=out_dtype, return_tanh=return_tanh, eval_mode=eval_mode,
             fast_path_semantics=fast_path_semantics, precise=precise, out=out, final_state=final_state,
             lam_tok=lam_tok, force_generic=force_generic)
-    if eval_mode != "clenshaw" or fast_path_semantics or return_tanh or out is not None or final_state is not None:
+    if eval_mode != "clenshaw" or return_tanh or out is not None or final_state is not None:
         raise NotImplementedError("orthossm_b200: the backward covers the Clenshaw forward with fresh outputs")
     H = coeffs.shape[1]
     lam = torch.as_tensor(lambda_per_head if lambda_per_head is not None else [ema_momentum] * H,
@@ -241,8 +241,40 @@ def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate
         lam_tok = gate_decay(x.detach(), gate_weight.detach(), gate_bias.detach(), lam, gate_scale=gate_scale,
                              gate_range=gate_range)
     opts = dict(ema_momentum=float(ema_momentum), out_dtype=out_dtype, precise=precise,
-                force_generic=force_generic)
+                force_generic=force_generic, fast_path_semantics=fast_path_semantics)
     return _ChebyEmaFn.apply(x, coeffs, init_state, lam, lam_tok, opts)
+
+
+def _rev_backward(x, g, coeffs, *, lam=None, momentum=0.9, lam_tok=None, init=None, want_init=False,
+                  segment=0, segment_coeffs=None, fastpath=False):
+    """ossm_cheby_ema_bwd: (grad_x f32, grad_coeffs f32, grad_init or None)."""
+    x = _rowmajor(x.detach())
+    if x.dtype not in _DT:
+        x = x.float()
+    B, S, D = x.shape
+    c = coeffs.detach().contiguous().float()
+    H, K, hd = c.shape[1], c.shape[2], c.shape[3]
+    g = g.float().contiguous()
+    gx = torch.empty(B, S, D, device=x.device, dtype=torch.float32)
+    gc = torch.empty_like(c)
+    gi = torch.empty(B, D, device=x.device) if want_init else None
+    init = None if init is None else init.detach().float().contiguous()
+    sc = None if segment_coeffs is None else segment_coeffs.detach().float().contiguous()
+    a = L.BwdArgs(B=B, S=S, H=H, head_dim=hd, degree=K, x=x.data_ptr(), x_dtype=_DT[x.dtype],
+                  x_stride_b=x.stride(0), x_stride_s=x.stride(1), coeffs=c.data_ptr(), lam_h=_ptr(lam),
+                  momentum=float(momentum), lam_tok=_ptr(lam_tok), init_state=_ptr(init), grad_out=g.data_ptr(),
+                  grad_out_dtype=L.OSSM_F32, grad_out_stride_b=g.stride(0), grad_out_stride_s=g.stride(1),
+                  grad_x=gx.data_ptr(), grad_x_dtype=L.OSSM_F32, grad_x_stride_b=gx.stride(0),
+                  grad_x_stride_s=gx.stride(1), grad_coeffs=gc.data_ptr(), grad_init=_ptr(gi),
+                  segment=int(segment), segment_coeffs=_ptr(sc), flags=L.OSSM_F_FASTPATH if fastpath else 0)
+    lib = L.lib()
+    nbytes = lib.ossm_bwd_workspace_bytes(L.C.byref(a))
+    if nbytes == 0:
+        L.check(L.OSSM_EINVAL, "backward (argument check)")
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    L.check(lib.ossm_cheby_ema_bwd(L.C.byref(a), ws.data_ptr(), nbytes,
+                                   torch.cuda.current_stream(x.device).cuda_stream), "cheby_ema_bwd")
+    return gx, gc, gi
 
 
 class _ChebyEmaFn(torch.autograd.Function):
@@ -255,39 +287,19 @@ class _ChebyEmaFn(torch.autograd.Function):
         ctx.save_for_backward(x, coeffs, init_state, lam, lam_tok)
         ctx.has_init = init_state is not None
         ctx.momentum = opts["ema_momentum"]
+        ctx.fastpath = bool(opts.get("fast_path_semantics"))
         return out, fin
 
     @staticmethod
     def backward(ctx, g_out, g_fin):
         x, coeffs, init_state, lam, lam_tok = ctx.saved_tensors
-        x = _rowmajor(x.detach())
-        if x.dtype not in _DT:
-            x = x.float()
         B, S, D = x.shape
-        c = coeffs.detach().contiguous().float()
-        H, K, hd = c.shape[1], c.shape[2], c.shape[3]
-        g = (torch.zeros(B, S, D, device=x.device) if g_out is None else g_out.float()).contiguous()
+        g = torch.zeros(B, S, D, device=x.device) if g_out is None else g_out.float().clone()
         if g_fin is not None:  # the final state is the last token's state
-            g = g.clone()
             g[:, -1] += g_fin.float()
-        gx = torch.empty(B, S, D, device=x.device, dtype=torch.float32)
-        gc = torch.empty_like(c)
-        gi = torch.empty(B, D, device=x.device) if ctx.has_init else None
-        init = None if init_state is None else init_state.detach().float().contiguous()
-        a = L.BwdArgs(B=B, S=S, H=H, head_dim=hd, degree=K, x=x.data_ptr(), x_dtype=_DT[x.dtype],
-                      x_stride_b=x.stride(0), x_stride_s=x.stride(1), coeffs=c.data_ptr(), lam_h=lam.data_ptr(),
-                      momentum=ctx.momentum, lam_tok=_ptr(lam_tok), init_state=_ptr(init), grad_out=g.data_ptr(),
-                      grad_out_dtype=L.OSSM_F32, grad_out_stride_b=g.stride(0), grad_out_stride_s=g.stride(1),
-                      grad_x=gx.data_ptr(), grad_x_dtype=L.OSSM_F32, grad_x_stride_b=gx.stride(0),
-                      grad_x_stride_s=gx.stride(1), grad_coeffs=gc.data_ptr(), grad_init=_ptr(gi))
-        lib = L.lib()
-        nbytes = lib.ossm_bwd_workspace_bytes(L.C.byref(a))
-        if nbytes == 0:
-            L.check(L.OSSM_EINVAL, "cheby_ema_forward backward (argument check)")
-        ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
-        L.check(lib.ossm_cheby_ema_bwd(L.C.byref(a), ws.data_ptr(), nbytes,
-                                       torch.cuda.current_stream(x.device).cuda_stream), "cheby_ema_bwd")
-        return gx.to(ctx.saved_tensors[0].dtype), gc.to(coeffs.dtype), gi, None, None, None
+        gx, gc, gi = _rev_backward(x, g, coeffs, lam=lam, momentum=ctx.momentum, lam_tok=lam_tok,
+                                   init=init_state, want_init=ctx.has_init, fastpath=ctx.fastpath)
+        return gx.to(x.dtype), gc.to(coeffs.dtype), gi, None, None, None
 
 
 def _cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,
@@ -513,9 +525,10 @@ def _per_batch(v, B, dev):
 
 def _lion_full_path(x, coeffs, momentum_buf, n_heads, base_lr, ema_momentum, lion_beta1,
                     lion_beta2, lion_wd, chunk_size, gate_global, dynamic_lambda, use_lut,
-                    out_dtype=torch.float32, final_state=None):
+                    out_dtype=torch.float32, final_state=None, trace=None):
     """All chunks of the reference's full path in one launch.  Returns
-    (out [B,S,D] bf16-rounded values, new coeffs, new momentum)."""
+    (out [B,S,D] bf16-rounded values, new coeffs, new momentum); ``trace``
+    ([n_chunks,B,H,K,hd] f32) receives the coefficients each chunk starts from."""
     _need_cuda(x, coeffs)
     x = _rowmajor(x)
     if x.dtype not in _DT:
@@ -542,15 +555,53 @@ def _lion_full_path(x, coeffs, momentum_buf, n_heads, base_lr, ema_momentum, lio
                    lut=_ptr(lut), out=out.data_ptr(), out_dtype=_DT[out_dtype],
                    out_stride_b=out.stride(0), out_stride_s=out.stride(1), tanh_out=None,
                    final_state=_ptr(final_state),
-                   flags=L.OSSM_EVAL_LUT if use_lut else L.OSSM_EVAL_CLENSHAW_DEG4)
+                   flags=L.OSSM_EVAL_LUT if use_lut else L.OSSM_EVAL_CLENSHAW_DEG4, coeff_trace=_ptr(trace))
     stream = torch.cuda.current_stream(dev)
     L.check(L.lib().ossm_cheby_rkv_lion(L.C.byref(a), stream.cuda_stream), "cheby_rkv_lion")
     return out, c, m
 
 
+class _RkvFullFn(torch.autograd.Function):
+    """The reference's full path (Lion TTT chunk by chunk) as one autograd node.
+
+    Gradients follow the reference's chunk loop (sdpc_kernel.py:2574-2606 with
+    FusedChebyRKVv10.backward, :2435-2515): each chunk's EMA restarts from zero,
+    so the adjoint is cut at every chunk start; each chunk is differentiated
+    against the coefficients it started from; the coefficients passed between
+    chunks are detached, so the input coefficients receive a gradient only when
+    the sequence is a single chunk."""
+
+    @staticmethod
+    def forward(ctx, x, coeffs, momentum_buf, opts):
+        B, S, _ = x.shape
+        chunk = int(opts["chunk_size"])
+        n_chunks = (S + chunk - 1) // chunk
+        trace = torch.empty((n_chunks,) + tuple(coeffs.shape), device=x.device, dtype=torch.float32)
+        out, c, m = _lion_full_path(x.detach(), coeffs.detach(), None if momentum_buf is None else momentum_buf.detach(),
+                                    opts["n_heads"], opts["base_lr"], opts["ema_momentum"], opts["lion_beta1"],
+                                    opts["lion_beta2"], opts["lion_wd"], chunk, opts["gate_global"],
+                                    opts["dynamic_lambda"], opts["use_lut"], trace=trace)
+        ctx.save_for_backward(x, coeffs, trace)
+        ctx.mu = float(opts["ema_momentum"])
+        ctx.chunk = chunk
+        ctx.mark_non_differentiable(c, m)
+        return out, c, m
+
+    @staticmethod
+    def backward(ctx, g_out, g_c, g_m):
+        x, coeffs, trace = ctx.saved_tensors
+        if g_out is None:
+            return None, None, None, None
+        single = trace.shape[0] == 1
+        gx, gc, _ = _rev_backward(x, g_out, trace[0], momentum=ctx.mu,
+                                  segment=0 if single else ctx.chunk, segment_coeffs=None if single else trace)
+        return gx.to(x.dtype), (gc.to(coeffs.dtype) if single else None), None, None
+
+
 class FusedChebyRKVv10(torch.autograd.Function):
     """One full-path call over the whole sequence as a single chunk
-    (reference: sdpc_kernel.py:2351-2515).  Same 16 positional arguments."""
+    (reference: sdpc_kernel.py:2351-2515).  Same 16 positional arguments;
+    backward as the reference's: gradients for x and coeffs."""
 
     @staticmethod
     def forward(ctx, x, coeffs, momentum_buf, n_heads=4, base_lr=0.005, ema_momentum=0.9,
@@ -558,15 +609,20 @@ class FusedChebyRKVv10(torch.autograd.Function):
                 gate_global=None, dynamic_lambda=None, use_lut=True, seq_threshold=384,
                 lion_max_norm=14.0):
         S = x.shape[1]
+        trace = torch.empty((1,) + tuple(coeffs.shape), device=x.device, dtype=torch.float32)
         out, c, m = _lion_full_path(x, coeffs, momentum_buf, n_heads, base_lr, ema_momentum,
                                     lion_beta1, lion_beta2, lion_wd, S, gate_global,
-                                    dynamic_lambda, use_lut)
+                                    dynamic_lambda, use_lut, trace=trace)
+        ctx.save_for_backward(x, coeffs)
+        ctx.mu = float(ema_momentum)
         ctx.mark_non_differentiable(c, m)
         return out, c, m
 
     @staticmethod
     def backward(ctx, grad_out, grad_c, grad_m):
-        raise NotImplementedError("orthossm_b200: backward of the Cheby-RKV op is not built yet")
+        x, coeffs = ctx.saved_tensors
+        gx, gc, _ = _rev_backward(x, grad_out, coeffs, momentum=ctx.mu)
+        return (gx.to(x.dtype), gc.to(coeffs.dtype)) + (None,) * 14
 
 
 def apply_cheby_rkv_v10(x, coeffs, momentum_buf, n_heads=4, base_lr=0.005, ema_momentum=0.9,
@@ -592,7 +648,10 @@ def apply_cheby_rkv_v10(x, coeffs, momentum_buf, n_heads=4, base_lr=0.005, ema_m
                                    out_dtype=torch.float32 if x.dtype != torch.bfloat16 else x.dtype)
         return out, coeffs, momentum_buf
     if torch.is_grad_enabled() and (x.requires_grad or coeffs.requires_grad):
-        raise NotImplementedError("orthossm_b200: backward of the Cheby-RKV op is not built yet")
+        opts = dict(n_heads=n_heads, base_lr=base_lr, ema_momentum=ema_momentum, lion_beta1=lion_beta1,
+                    lion_beta2=lion_beta2, lion_wd=lion_wd, chunk_size=min(int(chunk_size), S),
+                    gate_global=gate_global, dynamic_lambda=dynamic_lambda, use_lut=use_lut)
+        return _RkvFullFn.apply(x, coeffs, momentum_buf, opts)
     return _lion_full_path(x, coeffs, momentum_buf, n_heads, base_lr, ema_momentum, lion_beta1,
                            lion_beta2, lion_wd, chunk_size, gate_global, dynamic_lambda, use_lut)
 

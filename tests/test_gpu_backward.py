@@ -105,3 +105,89 @@ def test_backward_clamped_carried_state():
     assert relerr(ig.grad.cpu().numpy(), it.grad.numpy()) < 1e-4
     assert relerr(xg.grad.cpu().numpy(), xt.grad.numpy()) < 1e-4
     assert (ig.grad.cpu().numpy()[np.abs(ini) > 1.5] == 0).all()
+
+
+def torch_rkv_chunks(x, trace, mu, n_heads, chunk, fast=False):
+    """float64 forward of the reference's chunk loop with each chunk's own
+    coefficients (EMA from zero per chunk); fast: the fast path (x.sign(),
+    unclamped tanh)."""
+    B, S, D = x.shape
+    hd = D // n_heads
+    outs = []
+    for ci, t0 in enumerate(range(0, S, chunk)):
+        xc = x[:, t0:t0 + chunk]
+        c = trace[ci]
+        K = c.shape[2]
+        m = xc.abs().clamp(min=1e-7)
+        sgn = torch.sign(xc) if fast else torch.where(xc >= 0, torch.ones_like(xc), -torch.ones_like(xc))
+        xn = sgn * (1.0 - 1.0 / (1.0 + m))
+        T = [torch.ones_like(xn), xn]
+        for _ in range(2, K):
+            T.append(2.0 * xn * T[-1] - T[-2])
+        cc = c.permute(0, 2, 1, 3).reshape(B, K, D)
+        y = sum(cc[:, k][:, None, :] * T[k] for k in range(K))
+        gam = torch.tensor(np.repeat(R.gamma_h(n_heads), hd), dtype=torch.float64)
+        z = gam * y
+        u = torch.tanh(z) if fast else torch.tanh(torch.clamp(z, -4.0, 4.0))
+        s = torch.zeros(B, D, dtype=torch.float64)
+        for t in range(xc.shape[1]):
+            s = mu * s + (1.0 - mu) * u[:, t]
+            outs.append(s)
+    return torch.stack(outs, 1)
+
+
+@pytest.mark.parametrize("S,chunk,n_heads", [(600, 256, 4), (200, 256, 8)])
+def test_apply_cheby_rkv_v10_backward_matches_reference_semantics(S, chunk, n_heads):
+    """The full (Lion TTT) path: x always gets a gradient; coeffs only when the
+    sequence is one chunk (the reference detaches them between chunks)."""
+    import orthossm_b200 as O
+    from orthossm_b200.sdpc_kernel import _lion_full_path
+    B, D = 2, 512
+    hd = D // n_heads
+    x = det_normal((B, S, D), 1700).astype(np.float32)
+    c = spectral_coeffs(B, n_heads, 8, hd, 1701).astype(np.float32)
+    w = det_normal((B, S, D), 1702).astype(np.float32)
+    xg = torch.tensor(x, device="cuda", requires_grad=True)
+    cg = torch.tensor(c, device="cuda", requires_grad=True)
+    mom = torch.zeros_like(cg)
+    out, c_new, m_new = O.apply_cheby_rkv_v10(xg, cg, mom, n_heads=n_heads, chunk_size=chunk, seq_threshold=128)
+    (out * torch.tensor(w, device="cuda")).sum().backward()
+    n_chunks = (S + chunk - 1) // chunk
+    trace = torch.empty((n_chunks, B, n_heads, 8, hd), device="cuda")
+    with torch.no_grad():
+        _lion_full_path(torch.tensor(x, device="cuda"), torch.tensor(c, device="cuda"), torch.zeros_like(cg),
+                        n_heads, 0.005, 0.9, 0.9, 0.99, 0.01, min(chunk, S), None, None, True, trace=trace)
+    xt = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    tr = trace.cpu().double()
+    if n_chunks == 1:
+        tr = tr.clone().requires_grad_(True)
+    o = torch_rkv_chunks(xt, tr, 0.9, n_heads, min(chunk, S))
+    (o * torch.tensor(w, dtype=torch.float64)).sum().backward()
+    assert relerr(xg.grad.cpu().numpy(), xt.grad.numpy()) < 1e-4
+    if n_chunks == 1:
+        assert relerr(cg.grad.cpu().numpy(), tr.grad[0].numpy()) < 1e-4
+    else:
+        assert cg.grad is None
+
+
+def test_fast_path_backward():
+    """Below seq_threshold: the fast path (x.sign(), unclamped tanh); x and
+    coeffs get gradients."""
+    import orthossm_b200 as O
+    B, S, D, n_heads = 2, 100, 512, 8
+    hd = D // n_heads
+    x = det_normal((B, S, D), 1800).astype(np.float32)
+    x[0, 3, :5] = 0.0
+    c = spectral_coeffs(B, n_heads, 8, hd, 1801).astype(np.float32)
+    w = det_normal((B, S, D), 1802).astype(np.float32)
+    xg = torch.tensor(x, device="cuda", requires_grad=True)
+    cg = torch.tensor(c, device="cuda", requires_grad=True)
+    out, _, _ = O.apply_cheby_rkv_v10(xg, cg, torch.zeros_like(cg), n_heads=n_heads)
+    (out * torch.tensor(w, device="cuda")).sum().backward()
+    xt = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    ct = torch.tensor(c, dtype=torch.float64, requires_grad=True)
+    o = torch_rkv_chunks(xt, ct[None], 0.9, n_heads, S, fast=True)
+    (o * torch.tensor(w, dtype=torch.float64)).sum().backward()
+    assert relerr(out.detach().cpu().numpy(), o.detach().numpy()) < 1e-4
+    assert relerr(xg.grad.cpu().numpy(), xt.grad.numpy()) < 1e-4
+    assert relerr(cg.grad.cpu().numpy(), ct.grad.numpy()) < 1e-4
