@@ -103,7 +103,9 @@ template <bool PRECISE>
 OSSM_DEV float softsign(float x, bool torch_sem, float& xa, float& sgn) {
   const bool nan = x != x;
   const float xs = nan ? 0.0f : x;
-  const float m = fmaxf(fabsf(xs), 1e-7f);
+  // |x| is capped at 2^64, where m / (1 + m) is already 1 in fp32, so that
+  // +-inf and the largest finite inputs give +-1 as the reference's form does.
+  const float m = fminf(fmaxf(fabsf(xs), 1e-7f), 0x1p64f);
   // m / (1 + m) == 1 - 1/(1 + m) without the cancellation of the latter.
   xa = PRECISE ? __fdiv_rn(m, 1.0f + m) : m * rcp_fast(1.0f + m);
   sgn = xs >= 0.0f ? 1.0f : -1.0f;

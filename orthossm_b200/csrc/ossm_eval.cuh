@@ -91,8 +91,8 @@ OSSM_DEV float eval_u1(float x, const float (&c)[8], float gamma) {
 #pragma unroll
     for (int q = 6; q >= 0; --q) y = fmaf(y, xn, c[q]);
   }
-  if (EXACT) {
-    const float z = fminf(fmaxf(y, -4.f), 4.f);
+  if (EXACT) {  // a NaN y (from the coefficients) stays NaN, as in the reference's clamp (:1160-1161)
+    const float z = clamp4_nan(y);
     return x != x ? 0.f : (PRECISE ? tanhf(z) : tanh_fast(z));
   }
   const float z = clamp4_nan(y);
@@ -104,10 +104,17 @@ OSSM_DEV float2 eval_u(uint32_t raw, const float (&c0)[8], const float (&c1)[8],
                      eval_u1<PRECISE, EXACT>(__uint_as_float(raw & 0xffff0000u), c1, gamma));
 }
 
+OSSM_DEV float clamp1_nan(float v) {  // NaN-propagating clamp to [-1, 1]
+  float r;
+  asm("max.NaN.f32 %0, %1, 0fBF800000;\n\tmin.NaN.f32 %0, %0, 0f3F800000;" : "=f"(r) : "f"(v));
+  return r;
+}
+
 // s <- l s + (1 - l) u; token 0 of the sequence (first) folds the carried-in
-// state with the reference's clamp.
+// state with the reference's clamp.  The clamp lets NaN through, so a NaN u
+// of the fast evaluation still reaches the per-chunk check.
 OSSM_DEV float2 ema_step(float2 s, float2 lm, float2 u, bool first) {  // lm = (l, 1 - l)
-  if (first) return make_float2(clamp1(fmaf(lm.x, s.x, lm.y * u.x)), clamp1(fmaf(lm.x, s.y, lm.y * u.y)));
+  if (first) return make_float2(clamp1_nan(fmaf(lm.x, s.x, lm.y * u.x)), clamp1_nan(fmaf(lm.x, s.y, lm.y * u.y)));
   return fma2(make_float2(lm.x, lm.x), s, mul2(make_float2(lm.y, lm.y), u));
 }
 

@@ -63,6 +63,12 @@ struct FwdParams {
   uint32_t nctas;
 };
 
+OSSM_DEV float ev_clamp4(float v) {
+  float r;
+  asm("max.NaN.f32 %0, %1, 0fC0800000;\n\tmin.NaN.f32 %0, %0, 0f40800000;" : "=f"(r) : "f"(v));
+  return r;
+}
+
 struct GateParams {
   int B, S, H, D;
   const void* x;
@@ -278,7 +284,7 @@ __global__ void __launch_bounds__(kNT, 2) fwd_scan_kernel(const FwdParams p) {
       if (fastpath) {
         u[q] = tanhf(z);  // exact torch.tanh of the fast path (:1739)
       } else {
-        const float zc = fminf(fmaxf(z, -4.f), 4.f);
+        const float zc = ev_clamp4(z);  // NaN-propagating, as the reference's clamp (:1160-1161)
         u[q] = PRECISE ? tanhf(zc) : tanh_fast(zc);
         if (isnan_[q]) u[q] = 0.f;  // NaN guard (:1164)
       }

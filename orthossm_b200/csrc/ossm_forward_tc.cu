@@ -260,7 +260,10 @@ __global__ void __launch_bounds__(kNT, 2)
         xn.x = softsign<true>(x0, false, xa_, sg);
         xn.y = softsign<true>(x1, false, xa_, sg);
       } else {
-        xn = make_float2(x0 * rcp_fast(1.0f + fabsf(x0)), x1 * rcp_fast(1.0f + fabsf(x1)));  // x / (1 + |x|)
+        // x / (1 + |x|) with |x| capped at 2^64, so +-inf and |x| >= 2^126 give +-1
+        // (NaN is zeroed below)
+        const float m0 = fminf(fabsf(x0), 0x1p64f), m1 = fminf(fabsf(x1), 0x1p64f);
+        xn = make_float2(copysignf(m0 * rcp_fast(1.0f + m0), x0), copysignf(m1 * rcp_fast(1.0f + m1), x1));
       }
       float2 y;
       if (PRECISE) {

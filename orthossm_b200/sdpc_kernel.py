@@ -157,9 +157,9 @@ def _rowmajor(x):
 def _fwd_args(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None, gate_bias=None,
               gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None, out_dtype=None, return_tanh=False,
               eval_mode="clenshaw", fast_path_semantics=False, precise=None, out=None, final_state=None,
-              lam_tok=None, force_generic=False):
+              lam_tok=None, force_generic=False, extra_flags=0):
     """ossm_fwd_args for a forward call; returns (args, tensors to keep alive,
-    out, final_state)."""
+    out, final_state).  extra_flags: further OSSM_F_* kernel selections."""
     _need_cuda(x, coeffs)
     x = _rowmajor(x)
     if x.dtype not in _DT:
@@ -201,6 +201,7 @@ def _fwd_args(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=
         flags |= L.OSSM_F_PRECISE
     if force_generic:
         flags |= L.OSSM_F_GENERIC
+    flags |= int(extra_flags)
     lut = get_chebyshev_lut(dev) if eval_mode == "lut" else None
     a = L.FwdArgs(B=B, S=S, H=H, head_dim=hd, degree=K,
                   x=x.data_ptr(), x_dtype=_DT[x.dtype], x_stride_b=x.stride(0), x_stride_s=x.stride(1),
@@ -306,7 +307,7 @@ def _cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gat
                        gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None,
                        out_dtype=None, return_tanh=False, eval_mode="clenshaw",
                        fast_path_semantics=False, precise=None, out=None, final_state=None,
-                       lam_tok=None, force_generic=False):
+                       lam_tok=None, force_generic=False, extra_flags=0):
     """Fused softsign -> degree-K Chebyshev -> gamma_h -> tanh -> lambda-EMA.
 
     x: [B,S,D] float32 or bfloat16 (CUDA); coeffs: [B,H,K,hd] float32.
@@ -318,6 +319,8 @@ def _cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gat
     ``gate_decay``); overrides the gate.
     force_generic: run the generic kernel even where the TMA / tcgen05 path
     applies (bf16 x, head_dim 64); both compute the same function.
+    extra_flags: further OSSM_F_* kernel selections (e.g. OSSM_F_SINGLE_PASS),
+    all computing the same function.
     Returns (out [B,S,D] in out_dtype (default x.dtype), final_state [B,D] f32)
     and the f32 tanh cache when ``return_tanh``."""
     a, keep, out, final_state = _fwd_args(
@@ -325,7 +328,7 @@ def _cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gat
         gate_bias=gate_bias, gate_scale=gate_scale, gate_range=gate_range, init_state=init_state,
         out_dtype=out_dtype, return_tanh=return_tanh, eval_mode=eval_mode,
         fast_path_semantics=fast_path_semantics, precise=precise, out=out, final_state=final_state,
-        lam_tok=lam_tok, force_generic=force_generic)
+        lam_tok=lam_tok, force_generic=force_generic, extra_flags=extra_flags)
     tanh = keep[7]
     dev = out.device
     lib = L.lib()

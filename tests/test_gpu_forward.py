@@ -233,3 +233,37 @@ def test_final_state_is_last_output_fp32():
     c = T(spectral_coeffs(2, 4, 8, 64, 96))
     out, fin = run(x, c, ema_momentum=0.99)
     assert torch.equal(out[:, -1, :], fin)
+
+
+@pytest.mark.parametrize("path", ["default", "generic", "single_pass", "fp32_out"])
+def test_nan_inf_and_huge_inputs(path):
+    """The reference's fused semantics at non-finite and huge inputs
+    (sdpc_kernel.py:1078-1085, :1160-1164): NaN x contributes u = 0 (also at
+    token 0 of the sequence, where the carried-in state is folded in with a
+    clamp), +-inf and |x| near the bf16 maximum give xn = +-1."""
+    from orthossm_b200 import _lib as L
+    B, S, D, H = 4, 200, 512, 8
+    x = R.bf16_round(det_normal((B, S, D), 91)).astype(np.float32)
+    x[0, 5, 3] = np.nan
+    x[1, 17, 100] = np.inf
+    x[2, 150, 511] = -np.inf
+    x[3, 0, :7] = np.nan
+    x[3, 199, 64] = 3.0e38
+    x[2, 0, 8] = -np.inf
+    c = spectral_coeffs(B, H, 8, 64, 92).astype(np.float32)
+    init = det_normal((B, D), 93, 0.1).astype(np.float32)
+    lam = np.asarray(R.BASELINE_LAMBDA, np.float32)
+    kw = dict(lambda_per_head=lam.tolist(), init_state=T(init))
+    if path == "generic":
+        kw["force_generic"] = True
+    if path == "single_pass":
+        kw["extra_flags"] = L.OSSM_F_SINGLE_PASS
+    if path == "fp32_out":
+        kw["out_dtype"] = torch.float32
+    from orthossm_b200.sdpc_kernel import _cheby_ema_forward
+    out, fin = _cheby_ema_forward(T(x, torch.bfloat16), T(c), **kw)
+    ref = R.cheby_ema_forward(x, c, lam=f32(lam), init=init)
+    o = N(out)
+    assert np.isfinite(o).all() and np.isfinite(N(fin)).all()
+    assert relerr(o, ref["out"]) < BF16_TOL
+    assert relerr(N(fin), ref["final"]) < BF16_TOL
