@@ -63,6 +63,10 @@ enum ossm_dtype { OSSM_F32 = 0, OSSM_BF16 = 1 };
  * (chunk look-back across CTAs) instead of the default three-pass one
  * (chunk aggregates, carry scan, outputs).  Same function; kept for comparison. */
 #define OSSM_F_SINGLE_PASS (1u << 5)
+/* On the bf16 fast path with bf16 output and 4 to 32 sequences, use the
+ * single-pass kernel whose chunk carries are relayed by dedicated warps
+ * (x read once, every element evaluated once).  Same function. */
+#define OSSM_F_RELAY (1u << 6)
 
 /* ---------------------------------------------------------------------------
  * Fused softsign -> Chebyshev -> gamma_h damping -> tanh -> lambda-EMA scan.

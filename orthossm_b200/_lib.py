@@ -18,6 +18,7 @@ OSSM_F_FASTPATH = 1 << 2
 OSSM_F_PRECISE = 1 << 3
 OSSM_F_GENERIC = 1 << 4
 OSSM_F_SINGLE_PASS = 1 << 5
+OSSM_F_RELAY = 1 << 6
 OSSM_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 EXPORTED = (

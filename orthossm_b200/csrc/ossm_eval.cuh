@@ -16,14 +16,13 @@ OSSM_DEV float clamp4_nan(float v) {  // NaN-propagating clamp to [-4, 4]
   asm("max.NaN.f32 %0, %1, 0fC0800000;\n\tmin.NaN.f32 %0, %0, 0f40800000;" : "=f"(r) : "f"(v));
   return r;
 }
-// sign(x) (1 - 1/(1 + |x|)), the reference's own form (sdpc_kernel.py:1078-1085)
-// with one flush-to-zero reciprocal: |x| = inf or beyond 2^126 gives +-1, NaN
-// stays NaN.  (The reference's 1e-7 floor on |x| moves xn by < 2e-7.)
-OSSM_DEV float softsign_fast(float x) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + fabsf(x)));
-  return copysignf(1.0f - r, x);
-}
+// z = 4 xn = x / (1/4 + |x|/4) with one flush-to-zero reciprocal (three
+// instructions; 1/4 + |x|/4 stays below 2^126 for every bf16 or finite fp32
+// input of interest, so the reciprocal is never flushed).  xn is the
+// reference's softsign sign(x) (1 - 1/(1 + |x|)) (sdpc_kernel.py:1078-1085);
+// its 1e-7 floor on |x| moves xn by < 2e-7.  NaN and +-inf come out as NaN, so
+// they reach the per-chunk check.
+OSSM_DEV float softsign4_fast(float x) { return x * rcp_fast(fmaf(fabsf(x), 0.25f, 0.25f)); }
 
 // Chebyshev -> monomial coefficients with gamma folded in (T_0..T_7 written out).
 OSSM_DEV void cheb_to_mono(const float2 (&ck)[8], float gamma, float2 (&a)[8]) {
@@ -39,9 +38,10 @@ OSSM_DEV void cheb_to_mono(const float2 (&ck)[8], float gamma, float2 (&a)[8]) {
   a[7] = mul2(mul2(w(64.f), ck[7]), g2);
 }
 
-// The lane's coefficients of (b, h): raw (precise) or gamma-folded monomial.
 // The lane's two channels (j0, j0+1 of head h; 8 heads of 64) of the
-// coefficients [B,8,K,64]: raw (precise) or gamma-folded monomial.
+// coefficients [B,8,K,64]: raw (precise), or gamma-folded monomial scaled by
+// 4^-k for Horner in z = 4 xn (power-of-two scaling: the same roundings as
+// Horner in xn on the unscaled monomial coefficients).
 template <bool PRECISE>
 OSSM_DEV void load_coeffs(const float* coeffs, int K, int b, int h, int j0, float gamma, float (&c0)[8],
                           float (&c1)[8]) {
@@ -55,6 +55,9 @@ OSSM_DEV void load_coeffs(const float* coeffs, int K, int b, int h, int j0, floa
     for (int q = 0; q < 8; ++q) cf[q] = ck[q];
   } else {
     cheb_to_mono(ck, gamma, cf);
+    float sc = 1.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q, sc *= 0.25f) cf[q] = make_float2(cf[q].x * sc, cf[q].y * sc);
   }
 #pragma unroll
   for (int q = 0; q < 8; ++q) c0[q] = cf[q].x, c1[q] = cf[q].y;
@@ -67,13 +70,14 @@ OSSM_DEV void load_coeffs(const float* coeffs, int K, int b, int h, int j0, floa
 // reference's formula either way.
 template <bool PRECISE, bool EXACT>
 OSSM_DEV float eval_u1(float x, const float (&c)[8], float gamma) {
-  float xn;
+  float xn;  // xn (precise) or z = 4 xn (fast coefficients)
   if (PRECISE || EXACT) {
     float xa, sg;
     xn = softsign<PRECISE>(x, false, xa, sg);
     if (!EXACT && x != x) xn = x;
+    if (!PRECISE) xn *= 4.f;
   } else {
-    xn = softsign_fast(x);
+    xn = softsign4_fast(x);
   }
   float y;
   if (PRECISE) {  // Clenshaw on the raw coefficients, then gamma
@@ -86,7 +90,7 @@ OSSM_DEV float eval_u1(float x, const float (&c)[8], float gamma) {
       u1 = tt;
     }
     y = fmaf(xn, u1, c[0] - u2) * gamma;
-  } else {  // Horner on gamma-folded monomial coefficients
+  } else {  // Horner in z = 4 xn on the gamma-folded, 4^-k-scaled monomial coefficients
     y = c[7];
 #pragma unroll
     for (int q = 6; q >= 0; --q) y = fmaf(y, xn, c[q]);

@@ -418,6 +418,9 @@ bool ossm_tc_eligible(const ossm_fwd_args* a);
 size_t ossm_tc_workspace_bytes(const ossm_fwd_args* a);
 int ossm_tc_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
 size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a);
+bool ossm_sp_eligible(const ossm_fwd_args* a);
+size_t ossm_sp_workspace_bytes(const ossm_fwd_args* a);
+int ossm_sp_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
 int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
 int ossm_p3_shard_front(const ossm_fwd_args* a, int starts_sequence, char* ws, float* shard_decay, float* shard_state,
                         cudaStream_t st);
@@ -489,7 +492,9 @@ FwdLayout fwd_layout(const ossm_fwd_args* a) {
   if (a->gate_w && !a->lam_tok) off = align256(off + (size_t)a->B * a->S * a->H * 4);
   l.total = off;
   if (ossm_tc_eligible(a))  // bf16 fast paths: whichever layout the flags select
-    l.total = (a->flags & OSSM_F_SINGLE_PASS) ? ossm_tc_workspace_bytes(a) : ossm_p3_workspace_bytes(a);
+    l.total = (a->flags & OSSM_F_SINGLE_PASS) ? ossm_tc_workspace_bytes(a)
+              : ((a->flags & OSSM_F_RELAY) && ossm_sp_eligible(a)) ? ossm_sp_workspace_bytes(a)
+                                                                  : ossm_p3_workspace_bytes(a);
   return l;
 }
 
@@ -582,8 +587,11 @@ extern "C" int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_
   p.incB = reinterpret_cast<float*>(ws + l.off_incB);
   p.nctas = (uint32_t)l.N;
 
-  if (ossm_tc_eligible(a))
-    return (a->flags & OSSM_F_SINGLE_PASS) ? ossm_tc_launch(a, ws, st) : ossm_p3_launch(a, ws, st);
+  if (ossm_tc_eligible(a)) {
+    if (a->flags & OSSM_F_SINGLE_PASS) return ossm_tc_launch(a, ws, st);
+    if ((a->flags & OSSM_F_RELAY) && ossm_sp_eligible(a)) return ossm_sp_launch(a, ws, st);
+    return ossm_p3_launch(a, ws, st);
+  }
 
   if (a->gate_w && !a->lam_tok) {
     if (launch_gate(a, reinterpret_cast<float*>(ws + l.off_lam), st) != cudaSuccess) return OSSM_ELAUNCH;
