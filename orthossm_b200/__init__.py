@@ -11,4 +11,6 @@ from .sdpc_kernel import (  # noqa: F401
     init_chebyshev_coefficients, ttt_wpred_adam, workspace_status,
 )
 
+from .state import ChebyStreamState, StreamingChebyRKV  # noqa: F401
+
 __version__ = "0.1.0"
