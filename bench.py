@@ -12,6 +12,12 @@ weak scaling, no collective on the data path).  Rank 0 prints one JSON line.
 --impl reference times the oracle's C port (the reference algorithm on the
 host cores, all threads) on the same workload; under torchrun only rank 0
 runs it.
+
+--workload cfg5 times instead the config-5 LM forward (BASELINE.json
+configs[4]; orthossm_b200.lm): per GPU B=2 x S=65536 token ids, 6 V8 layers
+of d_model 512, vocab 32000, bf16.  Its JSON line reports tokens/s of the
+forward (value), of ids-in / loss-out through the model (e2e), and the share of
+the step spent in this package's Cheby-EMA kernels.
 """
 from __future__ import annotations
 
@@ -41,6 +47,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--soak-s", type=float, default=1.5, help="loaded seconds sampled for clocks before timing")
+    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2")
     ap.add_argument("--profile-once", action="store_true",
                     help="3 warm-up steps + 1 step, nothing else: for ncu")
     return ap.parse_args()
@@ -372,10 +379,134 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_lm(args):
+    """Config-5 LM forward (bf16), weak scaling over ranks (batch-parallel)."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    import orthossm_b200 as O
+    from orthossm_b200.lm import OrthoLMConfig, OrthoSSMLM, n_params
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    Bl, Sl = 2, 65536
+    cfg = OrthoLMConfig()
+    torch.manual_seed(42 + rank)
+    model = OrthoSSMLM(cfg).to(dev, torch.bfloat16).eval()
+    ids_pin = torch.randint(0, cfg.vocab_size, (Bl, Sl), dtype=torch.int64).pin_memory()
+    ids = ids_pin.to(dev)
+    states = model.fresh_states(Bl, dev, generator_seed=7 + rank)
+    stream = torch.cuda.Stream(dev)
+
+    def fwd(x):
+        return model(x, states)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.no_grad(), torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            fwd(ids)
+        torch.cuda.synchronize()
+        try:
+            gid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+        except Exception:
+            gid = str(local)
+        sampler = ClockSampler(gid)
+        sampler.start()
+        t_end = time.perf_counter() + args.soak_s  # loaded seconds for the clock samples
+        while time.perf_counter() < t_end:
+            fwd(ids)
+            stream.synchronize()
+        K_ = args.steps
+        barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(K_):
+            fwd(ids)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(ev0.elapsed_time(ev1))
+        clocks = sampler.stop()
+        # the Cheby-EMA kernels alone: one call per layer on the same shapes
+        h = torch.randn(Bl, Sl, cfg.d_model, device=dev).to(torch.bfloat16)
+        lam = model.layers[0].lam(dev)
+        gw, gb = model.layers[0].gate.weight.float(), model.layers[0].gate.bias.float()
+        c0 = states[0].coeffs
+        for _ in range(3):
+            O.cheby_ema_forward(h, c0, lambda_per_head=lam, gate_weight=gw, gate_bias=gb)
+        torch.cuda.synchronize()
+        c0e, c1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0e.record(stream)
+        for _ in range(cfg.n_layers * 5):
+            O.cheby_ema_forward(h, c0, lambda_per_head=lam, gate_weight=gw, gate_bias=gb)
+        c1e.record(stream)
+        torch.cuda.synchronize()
+        cheby_ms = c0e.elapsed_time(c1e) / 5
+        # end to end: token ids from pinned host memory, forward, loss back to the host
+        loss_pin = torch.empty((), dtype=torch.float32).pin_memory()
+        xdev = torch.empty_like(ids)
+        n_e2e = max(3, min(K_, 10))
+
+        def e2e_step():
+            xdev.copy_(ids_pin, non_blocking=True)
+            logits = fwd(xdev)
+            loss = F.cross_entropy(logits[:, :-1].reshape(-1, cfg.vocab_size).float(), xdev[:, 1:].reshape(-1))
+            loss_pin.copy_(loss, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    if rank == 0:
+        step_ms = ms / K_
+        print(json.dumps({
+            "metric": "tokens/sec", "value": world * Bl * Sl * K_ / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": K_, "warmup": max(args.warmup, 3), "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (token ids uniform over the vocab, random-init weights)",
+            "config": {"workload": f"cfg5: config-5 LM forward, per GPU B={Bl} x S={Sl}, d_model 512, 8 heads, "
+                                   f"6 V8 layers (Cheby-RKV + local attention window 512 + LayerNorm/Linear "
+                                   f"combine), vocab 32000, {n_params(model) / 1e6:.1f}M parameters",
+                       "global_batch": Bl * world, "seq_len": Sl, "parallelism": f"batch-sharded x{world}"},
+            "cheby_ema_ms_per_step": cheby_ms, "cheby_ema_share": cheby_ms / step_ms,
+            "e2e": {"value": world * Bl * Sl * n_e2e / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": Bl * Sl * 8, "d2h_bytes_per_step": 4},
+            "clocks": clocks, "device_status": O.workspace_status(),
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cfg5":
+        run_lm(args)
     else:
         run_ours(args)
 
