@@ -42,9 +42,10 @@ OSSM_DEV void cheb_to_mono(const float2 (&ck)[8], float gamma, float2 (&a)[8]) {
 // coefficients [B,8,K,64]: raw (precise), or gamma-folded monomial scaled by
 // 4^-k for Horner in z = 4 xn (power-of-two scaling: the same roundings as
 // Horner in xn on the unscaled monomial coefficients).
+// Held as (channel j0, channel j0+1) pairs, the operand layout of the packed
+// fp32x2 Horner.
 template <bool PRECISE>
-OSSM_DEV void load_coeffs(const float* coeffs, int K, int b, int h, int j0, float gamma, float (&c0)[8],
-                          float (&c1)[8]) {
+OSSM_DEV void load_coeffs(const float* coeffs, int K, int b, int h, int j0, float gamma, float2 (&m)[8]) {
   const float* cb = coeffs + ((size_t)(b * 8 + h) * K) * 64 + j0;
   float2 ck[8], cf[8];
 #pragma unroll
@@ -60,7 +61,7 @@ OSSM_DEV void load_coeffs(const float* coeffs, int K, int b, int h, int j0, floa
     for (int q = 0; q < 8; ++q, sc *= 0.25f) cf[q] = make_float2(cf[q].x * sc, cf[q].y * sc);
   }
 #pragma unroll
-  for (int q = 0; q < 8; ++q) c0[q] = cf[q].x, c1[q] = cf[q].y;
+  for (int q = 0; q < 8; ++q) m[q] = cf[q];
 }
 
 // u = tanh(clamp(gamma y(xn), +-4)) for one channel of one token.
@@ -69,7 +70,8 @@ OSSM_DEV void load_coeffs(const float* coeffs, int K, int b, int h, int j0, floa
 // comes out as NaN (caught per chunk); every other input takes the
 // reference's formula either way.
 template <bool PRECISE, bool EXACT>
-OSSM_DEV float eval_u1(float x, const float (&c)[8], float gamma) {
+OSSM_DEV float eval_u1(float x, const float2 (&m)[8], bool second, float gamma) {
+  auto c = [&](int q) { return second ? m[q].y : m[q].x; };
   float xn;  // xn (precise) or z = 4 xn (fast coefficients)
   if (PRECISE || EXACT) {
     float xa, sg;
@@ -82,18 +84,18 @@ OSSM_DEV float eval_u1(float x, const float (&c)[8], float gamma) {
   float y;
   if (PRECISE) {  // Clenshaw on the raw coefficients, then gamma
     const float x2 = 2.f * xn;
-    float u1 = c[7], u2 = 0.f;
+    float u1 = c(7), u2 = 0.f;
 #pragma unroll
     for (int q = 6; q >= 1; --q) {
-      const float tt = fmaf(x2, u1, c[q] - u2);
+      const float tt = fmaf(x2, u1, c(q) - u2);
       u2 = u1;
       u1 = tt;
     }
-    y = fmaf(xn, u1, c[0] - u2) * gamma;
+    y = fmaf(xn, u1, c(0) - u2) * gamma;
   } else {  // Horner in z = 4 xn on the gamma-folded, 4^-k-scaled monomial coefficients
-    y = c[7];
+    y = c(7);
 #pragma unroll
-    for (int q = 6; q >= 0; --q) y = fmaf(y, xn, c[q]);
+    for (int q = 6; q >= 0; --q) y = fmaf(y, xn, c(q));
   }
   if (EXACT) {  // a NaN y (from the coefficients) stays NaN, as in the reference's clamp (:1160-1161)
     const float z = clamp4_nan(y);
@@ -102,10 +104,20 @@ OSSM_DEV float eval_u1(float x, const float (&c)[8], float gamma) {
   const float z = clamp4_nan(y);
   return PRECISE ? tanhf(z) : tanh_fast(z);
 }
+// Both channels of one token.  The fast path runs its Horner on the channel
+// pair with packed fp32x2 FMAs (one instruction per degree for two channels).
 template <bool PRECISE, bool EXACT>
-OSSM_DEV float2 eval_u(uint32_t raw, const float (&c0)[8], const float (&c1)[8], float gamma) {
-  return make_float2(eval_u1<PRECISE, EXACT>(__uint_as_float(raw << 16), c0, gamma),
-                     eval_u1<PRECISE, EXACT>(__uint_as_float(raw & 0xffff0000u), c1, gamma));
+OSSM_DEV float2 eval_u(uint32_t raw, const float2 (&m)[8], float gamma) {
+  const float x0 = __uint_as_float(raw << 16), x1 = __uint_as_float(raw & 0xffff0000u);
+  if (!PRECISE && !EXACT) {
+    const float2 z = mul2(make_float2(x0, x1), make_float2(rcp_fast(fmaf(fabsf(x0), 0.25f, 0.25f)),
+                                                           rcp_fast(fmaf(fabsf(x1), 0.25f, 0.25f))));
+    float2 y = m[7];
+#pragma unroll
+    for (int q = 6; q >= 0; --q) y = fma2(y, z, m[q]);
+    return make_float2(tanh_fast(clamp4_nan(y.x)), tanh_fast(clamp4_nan(y.y)));
+  }
+  return make_float2(eval_u1<PRECISE, EXACT>(x0, m, false, gamma), eval_u1<PRECISE, EXACT>(x1, m, true, gamma));
 }
 
 OSSM_DEV float clamp1_nan(float v) {  // NaN-propagating clamp to [-1, 1]
@@ -125,11 +137,11 @@ OSSM_DEV float2 ema_step(float2 s, float2 lm, float2 u, bool first) {  // lm = (
 // The 32-token EMA of one chunk from state s (decays lam[0..31]); RAW(t) gives
 // the packed bf16 pair of token t, OUT(t, s) receives each state.
 template <bool PRECISE, bool EXACT, typename RawF, typename OutF>
-OSSM_DEV float2 ema_chunk(float2 s, const float2* lam, bool first, const float (&c0)[8], const float (&c1)[8],
-                          float gamma, RawF raw, OutF out) {
+OSSM_DEV float2 ema_chunk(float2 s, const float2* lam, bool first, const float2 (&m)[8], float gamma, RawF raw,
+                          OutF out) {
 #pragma unroll
   for (int t = 0; t < kL; ++t) {
-    s = ema_step(s, lam[t], eval_u<PRECISE, EXACT>(raw(t), c0, c1, gamma), t == 0 && first);
+    s = ema_step(s, lam[t], eval_u<PRECISE, EXACT>(raw(t), m, gamma), t == 0 && first);
     out(t, s);
   }
   return s;
@@ -137,11 +149,11 @@ OSSM_DEV float2 ema_chunk(float2 s, const float2* lam, bool first, const float (
 // The same with the reference's NaN / inf semantics as a rolled loop (the rare
 // recompute of a chunk that held such inputs).
 template <bool PRECISE, typename RawF, typename OutF>
-OSSM_DEV float2 ema_chunk_exact(float2 s, const float2* lam, bool first, const float (&c0)[8], const float (&c1)[8],
-                                float gamma, RawF raw, OutF out) {
+OSSM_DEV float2 ema_chunk_exact(float2 s, const float2* lam, bool first, const float2 (&m)[8], float gamma, RawF raw,
+                                OutF out) {
 #pragma unroll 1
   for (int t = 0; t < kL; ++t) {
-    s = ema_step(s, lam[t], eval_u<PRECISE, true>(raw(t), c0, c1, gamma), t == 0 && first);
+    s = ema_step(s, lam[t], eval_u<PRECISE, true>(raw(t), m, gamma), t == 0 && first);
     out(t, s);
   }
   return s;

@@ -113,8 +113,8 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
     for (int hh = 0; hh < kH; ++hh) tma_load_3d(sm + hh * kBox, &tmap_x, bar, hh * kHD, t0, b);
   }
   // while the tile lands: coefficients, gate weights, the caller's decay
-  float c0[8], c1[8];
-  load_coeffs<PRECISE>(p.coeffs, p.K, b, h, j0, gamma, c0, c1);
+  float2 cm[8];
+  load_coeffs<PRECISE>(p.coeffs, p.K, b, h, j0, gamma, cm);
   const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
   float lam = GATE ? lam_base : lam_token(p, p.lam_in, b, tg, h, lam_base);
   uint32_t whi[4][2], wlo[4][2];  // mma B fragments of W[gid][h*64 + ks*16 + ...], split bf16 hi + lo
@@ -189,12 +189,12 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
   for (int k = 0; k < 8; ++k) roff[k] = (uint32_t)((((lane >> 2) ^ k) << 4) + (lane & 3) * 4);
   auto raw = [&](int t) { return *reinterpret_cast<const uint32_t*>(xs + roff[t & 7] + t * 128); };
   auto none = [](int, float2) {};
-  s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, first, c0, c1, gamma, raw, none);
+  s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, none);
   if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y)) {  // NaN / inf inputs: the reference's semantics
     auto raw_t = [&](int t) {
       return *reinterpret_cast<const uint32_t*>(xs + box_off(t, lane >> 2) + (lane & 3) * 4);
     };
-    s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, first, c0, c1, gamma, raw_t, none);
+    s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, first, cm, gamma, raw_t, none);
   }
   const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
   *reinterpret_cast<float2*>(p.agg + n * kHD + j0) = s;
@@ -279,16 +279,16 @@ __global__ void __launch_bounds__(kSpans * 32) p3_carry_kernel(const Params p) {
 // immediate offset), all 32 tokens (FULL) or the ragged last chunk.
 template <bool PRECISE, typename OT, typename Stride>
 OSSM_DEV float2 out_chunk(const __nv_bfloat16* xp, OT* op, Stride xs, Stride os, float2 X, const float2* lam, bool first,
-                          const float (&c0)[8], const float (&c1)[8], float gamma) {
+                          const float2 (&cm)[8], float gamma) {
   uint32_t r[kL];
 #pragma unroll
   for (int t = 0; t < kL; ++t) r[t] = __ldcs(reinterpret_cast<const unsigned int*>(xp + t * xs));
   auto raw = [&](int t) { return r[t]; };
   auto emit = [&](int t, float2 v) { st2(op + t * os, sizeof(OT) == 4 ? make_float2(clamp1(v.x), clamp1(v.y)) : v); };
-  float2 s = ema_chunk<PRECISE, false>(X, lam, first, c0, c1, gamma, raw, emit);
+  float2 s = ema_chunk<PRECISE, false>(X, lam, first, cm, gamma, raw, emit);
   if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y)) {  // NaN / inf inputs: redo with the reference's semantics
     auto reraw = [&](int t) { return __ldcs(reinterpret_cast<const unsigned int*>(xp + t * xs)); };
-    s = ema_chunk_exact<PRECISE>(X, lam, first, c0, c1, gamma, reraw, emit);
+    s = ema_chunk_exact<PRECISE>(X, lam, first, cm, gamma, reraw, emit);
   }
   return s;
 }
@@ -296,13 +296,12 @@ OSSM_DEV float2 out_chunk(const __nv_bfloat16* xp, OT* op, Stride xs, Stride os,
 // with the reference's semantics throughout.
 template <bool PRECISE, typename OT>
 OSSM_DEV float2 out_chunk_general(const __nv_bfloat16* xp, OT* op, long long xs, long long os, int nt, float2 X,
-                                  const float2* lam, bool first, const float (&c0)[8], const float (&c1)[8],
-                                  float gamma) {
+                                  const float2* lam, bool first, const float2 (&cm)[8], float gamma) {
   auto raw = [&](int t) { return t < nt ? __ldcs(reinterpret_cast<const unsigned int*>(xp + t * xs)) : 0u; };
   auto emit = [&](int t, float2 v) {
     if (t < nt) st2(op + t * os, sizeof(OT) == 4 ? make_float2(clamp1(v.x), clamp1(v.y)) : v);
   };
-  return ema_chunk_exact<PRECISE>(X, lam, first, c0, c1, gamma, raw, emit);
+  return ema_chunk_exact<PRECISE>(X, lam, first, cm, gamma, raw, emit);
 }
 
 template <bool PRECISE, typename OT, bool CONTIG>
@@ -330,19 +329,19 @@ __global__ void __launch_bounds__(kNT, 3) p3_out_kernel(const Params p, const fl
   const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
   const float lam = lam_token(p, lam_tok, b, t0 + lane, h, lam_base);
   lam_s[h * kL + lane] = make_float2(lam, 1.f - lam);
-  float c0[8], c1[8];
-  load_coeffs<PRECISE>(p.coeffs, p.K, b, h, j0, gamma, c0, c1);
+  float2 cm[8];
+  load_coeffs<PRECISE>(p.coeffs, p.K, b, h, j0, gamma, cm);
   __syncwarp();
 
   const __nv_bfloat16* xp = p.x + (size_t)b * p.xsb + (size_t)t0 * p.xss + ch0;
   OT* op = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + (size_t)t0 * p.oss + ch0;
   float2 s;
   if (nt < kL)
-    s = out_chunk_general<PRECISE, OT>(xp, op, p.xss, p.oss, nt, X, lam_s + h * kL, first, c0, c1, gamma);
+    s = out_chunk_general<PRECISE, OT>(xp, op, p.xss, p.oss, nt, X, lam_s + h * kL, first, cm, gamma);
   else if (CONTIG)
-    s = out_chunk<PRECISE, OT>(xp, op, kD, kD, X, lam_s + h * kL, first, c0, c1, gamma);
+    s = out_chunk<PRECISE, OT>(xp, op, kD, kD, X, lam_s + h * kL, first, cm, gamma);
   else
-    s = out_chunk<PRECISE, OT>(xp, op, p.xss, p.oss, X, lam_s + h * kL, first, c0, c1, gamma);
+    s = out_chunk<PRECISE, OT>(xp, op, p.xss, p.oss, X, lam_s + h * kL, first, cm, gamma);
   // decays are 1 past the end, so the chunk's last state is the sequence's final state
   if (p.fin && t0 + kL >= p.S)
     *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) = make_float2(clamp1(s.x), clamp1(s.y));

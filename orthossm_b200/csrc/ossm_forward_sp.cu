@@ -329,10 +329,7 @@ OSSM_DEV bool work(const CUtensorMap* tmap, const Params& p, uint8_t* sm, int g,
   // coefficients: gamma-folded monomial, scaled by 4^-k for z = 4 xn
   float2 m[8];
   {
-    float c0[8], c1[8];
-    load_coeffs<false>(p.coeffs, p.K, b, h, j0, gamma, c0, c1);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) m[q] = make_float2(c0[q], c1[q]);
+    load_coeffs<false>(p.coeffs, p.K, b, h, j0, gamma, m);
   }
   const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
   float bias_h = 0.f;
