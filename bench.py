@@ -65,6 +65,16 @@ def peaks():
 # CPU baseline: the oracle's C port (reference algorithm), all host threads
 # ----------------------------------------------------------------------------
 
+def host_threads():
+    """Threads for the CPU legs: every core this process may run on.  (torchrun
+    sets OMP_NUM_THREADS=1 for its ranks, so OpenMP's own default would give
+    the reference arm one thread under N > 1.)"""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_sample(x_bits, c, W, b, init, lam, budget_s=8.0, max_reps=20):
     """Time the C port on the full per-GPU workload (one step = B*S tokens),
     repeated until ~budget_s of CPU time; returns (tokens/s, threads, sample)."""
@@ -72,7 +82,7 @@ def cpu_sample(x_bits, c, W, b, init, lam, budget_s=8.0, max_reps=20):
     from oracle import cref
     out = np.empty(x_bits.shape, np.uint16)
     fin = np.empty((x_bits.shape[0], x_bits.shape[2]), np.float32)
-    nth = cref.max_threads()
+    nth = host_threads()
     ts = []
     t_all = time.perf_counter()
     while len(ts) < max_reps and (time.perf_counter() - t_all) < budget_s:
@@ -114,7 +124,7 @@ def run_reference(args):
     c, W, b, init = small_inputs(1234)
     lam = np.asarray(LAMBDA, np.float32)
     from oracle import cref
-    nth = cref.max_threads()
+    nth = host_threads()
     out = np.empty(x_bits.shape, np.uint16)
     fin = np.empty((B, D), np.float32)
     for _ in range(max(args.warmup, 0)):
