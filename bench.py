@@ -328,26 +328,21 @@ def run_ours(args):
     # ---- end to end through the public API: pinned H2D, forward, D2H ----
     out_pin = torch.empty(B, S, D, dtype=torch.bfloat16).pin_memory()
     fin_pin = torch.empty(B, D).pin_memory()
-    xdev = torch.empty(B, S, D, device=dev, dtype=torch.bfloat16)
     e2e_steps = max(3, min(K_eff, 20))
+    def e2e_step():  # the public host-buffer call: copies in, forward, copies out, overlapped in parts
+        O.cheby_ema_forward_host(x_pin, c, lambda_per_head=lam, gate_weight=W, gate_bias=bvec, init_state=init,
+                                 out_host=out_pin, final_host=fin_pin)
+
     with torch.cuda.stream(stream):
         for _ in range(2):
-            xdev.copy_(x_pin, non_blocking=True)
-            o, f = O.cheby_ema_forward(xdev, c, lambda_per_head=lam, gate_weight=W, gate_bias=bvec,
-                                       init_state=init)
-            out_pin.copy_(o, non_blocking=True)
-            fin_pin.copy_(f, non_blocking=True)
+            e2e_step()
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(e2e_steps):
-            xdev.copy_(x_pin, non_blocking=True)
-            o, f = O.cheby_ema_forward(xdev, c, lambda_per_head=lam, gate_weight=W, gate_bias=bvec,
-                                       init_state=init)
-            out_pin.copy_(o, non_blocking=True)
-            fin_pin.copy_(f, non_blocking=True)
+            e2e_step()
         e1.record(stream)
     torch.cuda.synchronize()
     barrier()

@@ -423,6 +423,104 @@ def cheby_ema_forward_seqpar(x, coeffs, *, group=None, lambda_per_head=None, ema
 
 
 # ----------------------------------------------------------------------------
+# host-resident batches: copies overlapped with the forward
+# ----------------------------------------------------------------------------
+
+_HOST_STREAMS: dict = {}
+
+
+def _side_streams(dev):
+    with _WS_LOCK:
+        st = _HOST_STREAMS.get(dev)
+        if st is None:
+            st = _HOST_STREAMS[dev] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return st
+
+
+def cheby_ema_forward_host(x_host, coeffs, *, out_host=None, final_host=None, device=None, pieces=8, **kw):
+    """``cheby_ema_forward`` of a batch that lives in pinned host memory.
+
+    The batch goes through the GPU in ``pieces`` parts: groups of whole
+    sequences when there are at least two, else consecutive token ranges of
+    the one sequence (its EMA state carried from part to part).  Every host
+    slice is contiguous.  Three streams overlap the host-to-device copy of
+    part k+1, the forward of part k and the device-to-host copy of part k-1,
+    on two device buffers per direction; a PCIe link moves both directions at
+    once.  The current stream waits for all of it, so a later host read after
+    a synchronisation (or an event on the current stream) sees the results.
+
+    x_host: pinned CPU tensor [B, S, D] (bf16 or fp32); coeffs and the other
+    keyword arguments as for ``cheby_ema_forward`` (device tensors, or small
+    CPU ones, moved once).  Returns (out_host [B, S, D] in x's dtype unless
+    ``out_dtype`` says otherwise, final_host [B, D] fp32), both pinned."""
+    if x_host.is_cuda or not x_host.is_pinned():
+        raise ValueError("cheby_ema_forward_host: x_host must be a pinned CPU tensor")
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    B, S, D = x_host.shape
+    odt = kw.pop("out_dtype", None) or x_host.dtype
+    if out_host is None:
+        out_host = torch.empty(B, S, D, dtype=odt).pin_memory()
+    if final_host is None:
+        final_host = torch.empty(B, D, dtype=torch.float32).pin_memory()
+    mv = lambda t: t.to(dev, non_blocking=True) if isinstance(t, torch.Tensor) and not t.is_cuda else t  # noqa: E731
+    coeffs = mv(coeffs)
+    kw = {k: mv(v) for k, v in kw.items()}
+    init = kw.pop("init_state", None)
+    by_batch = B >= 2
+    n = max(1, min(int(pieces), B if by_batch else S))
+    cuts = [(B if by_batch else S) * i // n for i in range(n + 1)]
+    cur = torch.cuda.current_stream(dev)
+    s_in, s_cmp, s_out = _side_streams(dev)
+    big = max(b - a for a, b in zip(cuts[:-1], cuts[1:]))
+    shape = (big, S, D) if by_batch else (1, big, D)
+    xin = [torch.empty(shape, dtype=x_host.dtype, device=dev) for _ in range(2)]
+    yout = [torch.empty(shape, dtype=odt, device=dev) for _ in range(2)]
+    fin = [torch.empty((big if by_batch else 1), D, dtype=torch.float32, device=dev) for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(n)]
+    ev_cmp = [torch.cuda.Event() for _ in range(n)]
+    ev_out = [torch.cuda.Event() for _ in range(n)]
+    start = torch.cuda.Event()
+    start.record(cur)
+    for s_ in (s_in, s_cmp, s_out):
+        s_.wait_event(start)  # buffers, coefficients and init are ready on the current stream
+    for k in range(n):
+        i = k & 1
+        a, b = cuts[k], cuts[k + 1]
+        m = b - a
+        xh = x_host[a:b] if by_batch else x_host[:, a:b]
+        with torch.cuda.stream(s_in):
+            if k >= 2:
+                s_in.wait_event(ev_cmp[k - 2])  # buffer i was read by the forward of part k-2
+            xd = xin[i][:m] if by_batch else xin[i][:, :m]
+            xd.copy_(xh, non_blocking=True)
+            ev_in[k].record(s_in)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(ev_in[k])
+            if k >= 2:
+                s_cmp.wait_event(ev_out[k - 2])  # output buffer i was copied out after part k-2
+            yd = yout[i][:m] if by_batch else yout[i][:, :m]
+            if by_batch:
+                st_in = None if init is None else init[a:b]
+                cheby_ema_forward(xd, coeffs[a:b], init_state=st_in, out=yd, final_state=fin[i][:m],
+                                  out_dtype=odt, **kw)
+            else:
+                st_in = init if k == 0 else fin[i ^ 1]
+                cheby_ema_forward(xd, coeffs, init_state=st_in, out=yd, final_state=fin[i], out_dtype=odt, **kw)
+            ev_cmp[k].record(s_cmp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_cmp[k])
+            (out_host[a:b] if by_batch else out_host[:, a:b]).copy_(yd, non_blocking=True)
+            if by_batch:
+                final_host[a:b].copy_(fin[i][:m], non_blocking=True)
+            elif k == n - 1:
+                final_host.copy_(fin[i], non_blocking=True)
+            ev_out[k].record(s_out)
+    cur.wait_event(ev_out[n - 1])
+    cur.wait_event(ev_cmp[n - 1])
+    return out_host, final_host
+
+
+# ----------------------------------------------------------------------------
 # BASELINE-mode TTT: W_pred MSE objective + forget-gated Adam (BASELINE.json configs[3])
 # ----------------------------------------------------------------------------
 
