@@ -13,6 +13,12 @@ weak scaling, no collective on the data path).  Rank 0 prints one JSON line.
 host cores, all threads) on the same workload; under torchrun only rank 0
 runs it.
 
+--workload cfg3 times BASELINE.json configs[2]: one sequence of S=1,048,576
+tokens (bf16, fixed per-head decays, no gate) sharded along the sequence over
+the ranks (strong scaling; one NCCL all-gather of the shard totals).
+--workload cfg4 times configs[3]: the W_pred Adam TTT over B=4 x S=32768 per
+GPU in 2048-token chunks (weak scaling, batch-parallel).
+
 --workload cfg5 times instead the config-5 LM forward (BASELINE.json
 configs[4]; orthossm_b200.lm): per GPU B=2 x S=65536 token ids, 6 V8 layers
 of d_model 512, vocab 32000, bf16.  Its JSON line reports tokens/s of the
@@ -47,7 +53,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--soak-s", type=float, default=1.5, help="loaded seconds sampled for clocks before timing")
-    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2")
     ap.add_argument("--profile-once", action="store_true",
                     help="3 warm-up steps + 1 step, nothing else: for ncu")
     return ap.parse_args()
@@ -506,12 +512,157 @@ def run_lm(args):
         dist.destroy_process_group()
 
 
+def _dist_setup(timeout_s=300):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s), device_id=dev)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+    return world, rank, local, dev, max_over_ranks, barrier
+
+
+def _timed(fn, steps, warmup, stream, barrier, max_over_ranks):
+    """warm-up, then `steps` calls between CUDA events on `stream`; max over ranks (ms)."""
+    import torch
+    with torch.cuda.stream(stream):
+        for _ in range(max(warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    return max_over_ranks(e0.elapsed_time(e1))
+
+
+def run_cfg3(args):
+    """One 1,048,576-token sequence, sequence-sharded over the ranks."""
+    import torch
+    import torch.distributed as dist
+    import orthossm_b200 as O
+    world, rank, local, dev, mor, barrier = _dist_setup()
+    S_all = 1 << 20
+    Sl = S_all // world
+    g = torch.Generator().manual_seed(99)
+    x = torch.randn(1, S_all, D, generator=g)[:, rank * Sl:(rank + 1) * Sl].to(torch.bfloat16).contiguous().to(dev)
+    c = (torch.randn(1, H, K, HD, generator=g) / torch.arange(1, K + 1).view(1, 1, K, 1)).to(dev)
+    lam = torch.tensor(LAMBDA, device=dev)
+    out = torch.empty_like(x)
+    stream = torch.cuda.Stream(dev)
+    try:
+        gid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        gid = str(local)
+    sampler = ClockSampler(gid)
+    sampler.start()
+    if world > 1:
+        fn = lambda: O.cheby_ema_forward_seqpar(x, c, lambda_per_head=lam, out=out)  # noqa: E731
+    else:
+        fn = lambda: O.cheby_ema_forward(x, c, lambda_per_head=lam, out=out)  # noqa: E731
+    t_end = time.perf_counter() + args.soak_s
+    with torch.cuda.stream(stream):
+        while time.perf_counter() < t_end:
+            fn()
+            stream.synchronize()
+    ms = _timed(fn, args.steps, args.warmup, stream, barrier, mor)
+    clocks = sampler.stop()
+    if rank == 0:
+        step = ms / args.steps
+        bytes_step = S_all * D * 4  # x read + out written, whole sequence
+        peak, kind = peaks()
+        print(json.dumps({
+            "metric": "tokens/sec", "value": S_all / (step / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 compute (bf16 in/out)",
+            "data": "synthetic (seeded)",
+            "config": {"workload": "cfg3: one sequence of 1,048,576 tokens, D=512, degree 8, bf16 in/out, "
+                                   "per-head decays, no gate, sequence-sharded over the ranks",
+                       "global_batch": 1, "seq_len": S_all,
+                       "parallelism": f"sequence-sharded x{world} (one NCCL all-gather of shard totals)"},
+            "hbm_gbs_per_gpu": bytes_step / world / (step / 1e3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": bytes_step / world / (step / 1e3) / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": bytes_step / world / (step / 1e3) / 1e9 / peak, "peak_kind": kind},
+            "clocks": clocks, "device_status": O.workspace_status(),
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_cfg4(args):
+    """W_pred Adam TTT, B=4 x S=32768 per GPU, 2048-token chunks."""
+    import torch
+    import torch.distributed as dist
+    import orthossm_b200 as O
+    world, rank, local, dev, mor, barrier = _dist_setup()
+    Bl, Sl, chunk = 4, 32768, 2048
+    g = torch.Generator().manual_seed(7 + rank)
+    x = torch.randn(Bl, Sl, D, generator=g).to(torch.bfloat16).to(dev)
+    c = (torch.randn(Bl, H, K, HD, generator=g) / torch.arange(1, K + 1).view(1, 1, K, 1)).to(dev)
+    Wp = (torch.randn(D, D, generator=g) * 0.02).to(dev)
+    m, v = torch.zeros_like(c), torch.zeros_like(c)
+    lam = torch.tensor(LAMBDA, device=dev)
+    stream = torch.cuda.Stream(dev)
+    fn = lambda: O.ttt_wpred_adam(x, c, m, v, 0, Wp, lambda_per_head=lam, chunk=chunk)  # noqa: E731
+    try:
+        gid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        gid = str(local)
+    sampler = ClockSampler(gid)
+    sampler.start()
+    t_end = time.perf_counter() + args.soak_s
+    with torch.cuda.stream(stream):
+        while time.perf_counter() < t_end:
+            fn()
+            stream.synchronize()
+    ms = _timed(fn, args.steps, args.warmup, stream, barrier, mor)
+    clocks = sampler.stop()
+    if rank == 0:
+        step = ms / args.steps
+        flops = Bl * Sl * 2 * 2 * D * D  # W_pred s and W_pred^T r per token
+        print(json.dumps({
+            "metric": "tokens/sec", "value": world * Bl * Sl / (step / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 compute (bf16 x), fp32 state and GEMMs",
+            "data": "synthetic (seeded)",
+            "config": {"workload": "cfg4: W_pred MSE TTT with forget-gated Adam, per GPU B=4 x S=32768, "
+                                   "2048-token chunks (16 sequential steps), W_pred 512x512",
+                       "global_batch": Bl * world, "seq_len": Sl, "parallelism": f"batch-sharded x{world}"},
+            "gemm_tflops": flops / (step / 1e3) / 1e12,
+            "clocks": clocks, "device_status": O.workspace_status(),
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "cfg5":
         run_lm(args)
+    elif args.workload == "cfg3":
+        run_cfg3(args)
+    elif args.workload == "cfg4":
+        run_cfg4(args)
     else:
         run_ours(args)
 

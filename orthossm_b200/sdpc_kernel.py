@@ -524,9 +524,26 @@ def cheby_ema_forward_host(x_host, coeffs, *, out_host=None, final_host=None, de
 # BASELINE-mode TTT: W_pred MSE objective + forget-gated Adam
 # ----------------------------------------------------------------------------
 
+class _matmul_precision:
+    """fp32 matmuls on TF32 tensor cores ("tf32") or in full fp32 ("fp32") for
+    the enclosed calls; the caller's setting is restored on exit."""
+
+    def __init__(self, mode):
+        if mode not in ("tf32", "fp32"):
+            raise ValueError(f"gemm must be 'tf32' or 'fp32', got {mode!r}")
+        self.mode = mode
+
+    def __enter__(self):
+        self.prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = self.mode == "tf32"
+
+    def __exit__(self, *exc):
+        torch.backends.cuda.matmul.allow_tf32 = self.prev
+
+
 def ttt_wpred_adam(x, coeffs, m, v, step, W_pred, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,
                    gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None, chunk=2048,
-                   lr=1e-3, betas=(0.9, 0.999), eps=1e-8, spectral_pow=2.0, forget=True):
+                   lr=1e-3, betas=(0.9, 0.999), eps=1e-8, spectral_pow=2.0, forget=True, gemm="tf32"):
     """Chunked forward + test-time training of the Chebyshev coefficients.
 
     For each chunk of ``chunk`` tokens: the forward with the chunk-start
@@ -534,8 +551,10 @@ def ttt_wpred_adam(x, coeffs, m, v, step, W_pred, *, lambda_per_head=None, ema_m
     mean_{t<L-1,d} (W_pred s_t - x_{t+1})^2 per sequence, its gradient through
     the EMA, tanh and Chebyshev basis, scaled by 1/(k+1)^spectral_pow, and one
     Adam step with the forget gate c <- lambda_h c - lr mhat/(sqrt(vhat)+eps).
-    The W_pred products run on cuBLAS (fp32); the adjoint, gradient and Adam
-    run in ``ossm_ttt_wpred_step``.
+    The W_pred products run on cuBLAS: ``gemm="tf32"`` (default) on the tensor
+    cores with fp32 inputs and accumulation rounded through TF32, as the
+    spec's "BF16/TF32 GEMM" allows; ``gemm="fp32"`` keeps full fp32 (SIMT).
+    The adjoint, gradient and Adam run in ``ossm_ttt_wpred_step``.
 
     x: [B,S,D] (CUDA, bf16 or fp32); coeffs, m, v: [B,H,K,hd] (not modified);
     step: Adam steps already taken.  Returns dict(out [B,S,D] fp32, coeffs, m,
@@ -567,8 +586,9 @@ def ttt_wpred_adam(x, coeffs, m, v, step, W_pred, *, lambda_per_head=None, ema_m
                                    out_dtype=torch.float32, out=out[:, t0:t0 + Lc])
         gs = None
         if Lc > 1:
-            r = torch.matmul(s[:, :-1], Wp.t()) - xc[:, 1:].float()
-            gs = torch.matmul(r, Wp).mul_(2.0 / ((Lc - 1) * D)).contiguous()
+            with _matmul_precision(gemm):
+                r = torch.matmul(s[:, :-1], Wp.t()) - xc[:, 1:].float()
+                gs = torch.matmul(r, Wp).mul_(2.0 / ((Lc - 1) * D)).contiguous()
         step += 1
         a = L.TttArgs(B=B, L=Lc, H=H, head_dim=hd, degree=K, x=xc.data_ptr(), x_dtype=_DT[xdt],
                       x_stride_b=xc.stride(0), x_stride_s=xc.stride(1), coeffs=c.data_ptr(), m=m.data_ptr(),
