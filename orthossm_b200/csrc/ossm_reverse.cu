@@ -46,6 +46,7 @@ namespace rev {
 
 constexpr int kL = 32;  // tokens per sub-chunk
 constexpr int kMaxK = 8;
+constexpr int kB = 8;  // tokens (or sub-chunks) whose loads are issued together
 
 struct Params {
   int B, L, H, HD, K, nq, ngrp;  // ngrp: 64-channel groups per head (one warp each)
@@ -122,13 +123,25 @@ __global__ void __launch_bounds__(256) rev_agg_kernel(const Params p) {
   const int t0 = q * kL;
   float R[2] = {0.f, 0.f};
   float A = 1.f;
-  for (int t = min(t0 + kL, p.L) - 1; t >= t0; --t) {
-    const float an = carry_decay(p, b, t + 1, h);  // a_{t+1}
-    A *= an;
+  // tokens in batches of kB: the batch's loads first (independent), then the fold
+  for (int tb = min(t0 + kL, p.L) - 1; tb >= t0; tb -= kB) {
+    float anv[kB], gv[2][kB];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int j = jb + 32 * e;
-      if (j < p.HD) R[e] = fmaf(an, R[e], gval(p, b, t, h * p.HD + j));
+    for (int i = 0; i < kB; ++i) {
+      const int t = tb - i;
+      anv[i] = t >= t0 ? carry_decay(p, b, t + 1, h) : 1.f;  // a_{t+1}
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = jb + 32 * e;
+        gv[e][i] = (t >= t0 && j < p.HD) ? gval(p, b, t, h * p.HD + j) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      if (tb - i < t0) break;
+      A *= anv[i];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) R[e] = fmaf(anv[i], R[e], gv[e][i]);
     }
   }
 #pragma unroll
@@ -145,14 +158,29 @@ __global__ void __launch_bounds__(32) rev_carry_kernel(const Params p) {
   const int bh = blockIdx.x / p.ngrp, lane = threadIdx.x;
   const int jb = (blockIdx.x % p.ngrp) * 64 + lane;
   float C[2] = {0.f, 0.f};
-  for (int q = p.nq - 1; q >= 0; --q) {
-    const float A = p.Aq[(size_t)bh * p.nq + q];
+  for (int qb = p.nq - 1; qb >= 0; qb -= kB) {  // kB sub-chunks' records first, then the fold
+    float Av[kB], Rv[2][kB];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int j = jb + 32 * e;
-      if (j < p.HD) {
-        p.Cq[((size_t)bh * p.nq + q) * p.HD + j] = C[e];
-        C[e] = fmaf(A, C[e], p.Rq[((size_t)bh * p.nq + q) * p.HD + j]);
+    for (int i = 0; i < kB; ++i) {
+      const int q = qb - i;
+      Av[i] = q >= 0 ? p.Aq[(size_t)bh * p.nq + q] : 1.f;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = jb + 32 * e;
+        Rv[e][i] = (q >= 0 && j < p.HD) ? p.Rq[((size_t)bh * p.nq + q) * p.HD + j] : 0.f;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int q = qb - i;
+      if (q < 0) break;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = jb + 32 * e;
+        if (j < p.HD) {
+          p.Cq[((size_t)bh * p.nq + q) * p.HD + j] = C[e];
+          C[e] = fmaf(Av[i], C[e], Rv[e][i]);
+        }
       }
     }
   }
