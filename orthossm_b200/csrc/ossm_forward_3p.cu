@@ -82,6 +82,14 @@ struct Params {
   const float* carry_in;  // [B][D] state entering the shard (or NULL: zero / init_state)
 };
 
+// w = hi + lo with hi = bf16(w) and lo = bf16(w - hi), for a pair of weights,
+// with packed conversions only (the scalar float -> bf16 conversion would
+// take the MUFU pipe the evaluation is bound by).
+OSSM_DEV void split_bf16x2(float2 w, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16x2(w.x, w.y);
+  lo = pack_bf16x2(w.x - __uint_as_float(hi << 16), w.y - __uint_as_float(hi & 0xffff0000u));
+}
+
 // Decay of token (t0 + lane), head h, from a per-token input or the constant.
 OSSM_DEV float lam_token(const Params& p, const float* lam_tok, int b, int tg, int h, float lam_base) {
   if (tg >= p.S) return 1.f;  // past the end: the state is carried unchanged
@@ -126,17 +134,8 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
       const float* wr = p.gate_w + (size_t)gid * kD + h * kHD + ks * 16 + 2 * tig;
       const float2 w01 = __ldg(reinterpret_cast<const float2*>(wr));
       const float2 w89 = __ldg(reinterpret_cast<const float2*>(wr + 8));
-      const float hw[4] = {w01.x, w01.y, w89.x, w89.y};
-      __nv_bfloat16 hi[4], lo[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        hi[q] = __float2bfloat16_rn(hw[q]);
-        lo[q] = __float2bfloat16_rn(hw[q] - __bfloat162float(hi[q]));
-      }
-      whi[ks][0] = pack_bf16x2(__bfloat162float(hi[0]), __bfloat162float(hi[1]));
-      whi[ks][1] = pack_bf16x2(__bfloat162float(hi[2]), __bfloat162float(hi[3]));
-      wlo[ks][0] = pack_bf16x2(__bfloat162float(lo[0]), __bfloat162float(lo[1]));
-      wlo[ks][1] = pack_bf16x2(__bfloat162float(lo[2]), __bfloat162float(lo[3]));
+      split_bf16x2(w01, whi[ks][0], wlo[ks][0]);
+      split_bf16x2(w89, whi[ks][1], wlo[ks][1]);
     }
     bias_h = __ldg(p.gate_b + h);
   }
