@@ -12,9 +12,11 @@
 //                    held in registers), evaluates u and runs the EMA from a zero
 //                    state.  Writes the chunk's end state and decay product (and
 //                    the per-token decays when gated).
-//   p3_carry_kernel  one CTA per (b, h) chain: the carry into every chunk,
-//                    c_k = A_{k-1} c_{k-1} + agg_{k-1}, in a fixed order
-//                    (16 spans folded in parallel, then across spans).
+//   p3_carry_kernel  one CTA per (b, h) chain and block of 512 chunks: the
+//                    carry into every chunk, c_k = A_{k-1} c_{k-1} + agg_{k-1},
+//                    in a fixed order (32 spans of 16 chunks folded in
+//                    parallel, then across spans); p3_blockfold_kernel joins
+//                    the blocks of chains longer than one block.
 //   p3_out_kernel    one CTA per (b, chunk), warp = head: re-reads x, evaluates
 //                    u again and runs the EMA from the chunk's carry, writing
 //                    each output as it is produced.
@@ -53,7 +55,9 @@ constexpr int kOffPart = kTile;                       // [8 warps][32 tokens][8]
 constexpr int kOffLam = kOffPart + kH * kL * kH * 4;  // [8 heads][32] float2 (l, 1 - l)
 constexpr int kOffBar = kOffLam + kH * kL * 8;
 constexpr int kAggSmem = kOffBar + 16 + 1024;        // + alignment slack
-constexpr int kSpans = 32;                           // carry kernel: warps per chain
+constexpr int kSpans = 32;                           // carry kernel: warps per block
+constexpr int kPer = 16;                             // carry kernel: chunks per warp
+constexpr int kBlk = kSpans * kPer;                  // chunks per carry block
 
 struct Params {
   int B, S, K, nchunks;
@@ -73,8 +77,13 @@ struct Params {
   long long osb, oss;
   float* A;      // [N] chunk decay products
   float* agg;    // [N][64] chunk end states from zero (chunk 0: from the carried-in state)
-  float* carry;  // [N][64] state entering each chunk (from a zero state at the shard start)
-  float* P;      // [N] decay product from the shard start to each chunk's start
+  float* carry;  // [N][64] state entering each chunk (from a zero state at its carry block's start)
+  float* P;      // [N] decay product from the carry block's start to each chunk's start
+  int nblk;      // carry blocks per chain (kBlk chunks each)
+  float* blk_A;  // [B*H*nblk] block decay products
+  float* blk_E;  // [B*H*nblk][64] block end states from a zero state
+  float* blk_X;  // [B*H*nblk][64] state entering each block (from a zero state at the shard start)
+  float* blk_P;  // [B*H*nblk] decay product from the shard start to each block's start
   WsHeader* ws;  // sticky status (a tile that never arrived)
   int starts_seq;         // this call's first token is token 0 of the sequence
   float* tot_A;           // [B*H] shard decay products (or NULL)
@@ -202,7 +211,11 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------------------
-// pass 2: carries (one CTA per (b, h) chain; warp w folds span w, lane = 2 channels)
+// pass 2: carries.  A chain's chunks are cut into blocks of kBlk; one CTA per
+// (chain, block), warp w folds the block's span w of kPer chunks, lane = 2
+// channels.  Each warp loads its whole span at once and keeps it in registers
+// for the second fold, so the kernel makes one round trip to memory.  With
+// more than one block per chain a second small kernel joins the blocks.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kSpans * 32) p3_carry_kernel(const Params p) {
   __shared__ float2 spanB[kSpans][32];
@@ -210,32 +223,30 @@ __global__ void __launch_bounds__(kSpans * 32) p3_carry_kernel(const Params p) {
   __shared__ float2 spanX[kSpans][32];
   __shared__ float spanP[kSpans];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t n0 = (size_t)blockIdx.x * p.nchunks;
-  const int per = (p.nchunks + kSpans - 1) / kSpans;
-  const int c0 = min(w * per, p.nchunks), c1 = min(c0 + per, p.nchunks);
-  // span aggregate: state after the span from zero, and its decay product
-  float2 B = make_float2(0.f, 0.f);
+  const int chain = (int)(blockIdx.x / p.nblk), blk = (int)(blockIdx.x - (unsigned)chain * p.nblk);
+  const size_t n0 = (size_t)chain * p.nchunks;
+  const int c0 = blk * kBlk + w * kPer, cnt = max(0, min(kPer, p.nchunks - c0));
+  // the span's decays and aggregates; past the end a decay of 1 and a zero
+  // aggregate leave every fold unchanged
+  float Ac[kPer];
+  float2 g[kPer];
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const bool in = q < cnt;
+    Ac[q] = in ? __ldg(p.A + n0 + c0 + q) : 1.f;
+    g[q] = in ? __ldg(reinterpret_cast<const float2*>(p.agg + (n0 + c0 + q) * kHD) + lane) : make_float2(0.f, 0.f);
+  }
+  float2 B = make_float2(0.f, 0.f);  // span aggregate: state after the span from zero, and its decay product
   float A = 1.f;
-  for (int cb = c0; cb < c1; cb += 8) {  // loads of 8 chunks first, then the fold
-    float Ac[8];
-    float2 g[8];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int cc = min(cb + q, c1 - 1);
-      Ac[q] = __ldg(p.A + n0 + cc);
-      g[q] = __ldg(reinterpret_cast<const float2*>(p.agg + (n0 + cc) * kHD) + lane);
-    }
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-      if (cb + q < c1) {
-        B = make_float2(fmaf(Ac[q], B.x, g[q].x), fmaf(Ac[q], B.y, g[q].y));
-        A *= Ac[q];
-      }
+  for (int q = 0; q < kPer; ++q) {
+    B = make_float2(fmaf(Ac[q], B.x, g[q].x), fmaf(Ac[q], B.y, g[q].y));
+    A *= Ac[q];
   }
   spanB[w][lane] = B;
   if (lane == 0) spanA[w] = A;
   __syncthreads();
-  if (w == 0) {  // carries into the spans, in span order; the chain's totals
+  if (w == 0) {  // carries into the spans, in span order; the block's totals
     float2 X = make_float2(0.f, 0.f);
     float P = 1.f;
     for (int q = 0; q < kSpans; ++q) {
@@ -244,30 +255,56 @@ __global__ void __launch_bounds__(kSpans * 32) p3_carry_kernel(const Params p) {
       X = make_float2(fmaf(spanA[q], X.x, spanB[q][lane].x), fmaf(spanA[q], X.y, spanB[q][lane].y));
       P *= spanA[q];
     }
-    if (p.tot_E) reinterpret_cast<float2*>(p.tot_E + (size_t)blockIdx.x * kHD)[lane] = X;
-    if (p.tot_A && lane == 0) p.tot_A[blockIdx.x] = P;
+    if (p.nblk > 1) {
+      const size_t k = (size_t)chain * p.nblk + blk;
+      reinterpret_cast<float2*>(p.blk_E + k * kHD)[lane] = X;
+      if (lane == 0) p.blk_A[k] = P;
+    } else {
+      if (p.tot_E) reinterpret_cast<float2*>(p.tot_E + (size_t)chain * kHD)[lane] = X;
+      if (p.tot_A && lane == 0) p.tot_A[chain] = P;
+    }
   }
   __syncthreads();
   float2 X = spanX[w][lane];
   float Pc = spanP[w];
-  for (int cb = c0; cb < c1; cb += 8) {
-    float Ac[8];
-    float2 g[8];
+#pragma unroll
+  for (int q = 0; q < kPer; ++q)
+    if (q < cnt) {
+      reinterpret_cast<float2*>(p.carry + (n0 + c0 + q) * kHD)[lane] = X;
+      if (lane == 0) p.P[n0 + c0 + q] = Pc;
+      X = make_float2(fmaf(Ac[q], X.x, g[q].x), fmaf(Ac[q], X.y, g[q].y));
+      Pc *= Ac[q];
+    }
+}
+
+// The state entering each block of a chain (from a zero state at the shard
+// start) and the decay product up to it, folded in block order; the chain's
+// totals.  One warp per chain, lane = 2 channels, loads 8 blocks at a time.
+__global__ void __launch_bounds__(32) p3_blockfold_kernel(const Params p) {
+  const int chain = blockIdx.x, lane = threadIdx.x;
+  const size_t k0 = (size_t)chain * p.nblk;
+  float2 X = make_float2(0.f, 0.f);
+  float P = 1.f;
+  for (int kb = 0; kb < p.nblk; kb += 8) {
+    float Ab[8];
+    float2 E[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const int cc = min(cb + q, c1 - 1);
-      Ac[q] = __ldg(p.A + n0 + cc);
-      g[q] = __ldg(reinterpret_cast<const float2*>(p.agg + (n0 + cc) * kHD) + lane);
+      const size_t k = k0 + min(kb + q, p.nblk - 1);
+      Ab[q] = __ldg(p.blk_A + k);
+      E[q] = __ldg(reinterpret_cast<const float2*>(p.blk_E + k * kHD) + lane);
     }
 #pragma unroll
     for (int q = 0; q < 8; ++q)
-      if (cb + q < c1) {
-        reinterpret_cast<float2*>(p.carry + (n0 + cb + q) * kHD)[lane] = X;
-        if (lane == 0) p.P[n0 + cb + q] = Pc;
-        X = make_float2(fmaf(Ac[q], X.x, g[q].x), fmaf(Ac[q], X.y, g[q].y));
-        Pc *= Ac[q];
+      if (kb + q < p.nblk) {
+        reinterpret_cast<float2*>(p.blk_X + (k0 + kb + q) * kHD)[lane] = X;
+        if (lane == 0) p.blk_P[k0 + kb + q] = P;
+        X = make_float2(fmaf(Ab[q], X.x, E[q].x), fmaf(Ab[q], X.y, E[q].y));
+        P *= Ab[q];
       }
   }
+  if (p.tot_E) reinterpret_cast<float2*>(p.tot_E + (size_t)chain * kHD)[lane] = X;
+  if (p.tot_A && lane == 0) p.tot_A[chain] = P;
 }
 
 // ---------------------------------------------------------------------------
@@ -319,10 +356,21 @@ __global__ void __launch_bounds__(kNT, 3) p3_out_kernel(const Params p, const fl
     X = p.init ? __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + ch0)) : make_float2(0.f, 0.f);
   } else {
     X = c == 0 ? make_float2(0.f, 0.f) : *reinterpret_cast<const float2*>(p.carry + n * kHD + j0);
-    if (p.carry_in) {  // the state entering the shard, decayed to this chunk
+    const int blk = c / kBlk;
+    if (blk > 0 || p.carry_in) {  // the state entering the chunk's block, decayed to this chunk
+      const size_t k = (size_t)(b * kH + h) * p.nblk + blk;
+      float2 Y = make_float2(0.f, 0.f);
+      float Pb = 1.f;
+      if (blk > 0) {
+        Y = *reinterpret_cast<const float2*>(p.blk_X + k * kHD + j0);
+        Pb = p.blk_P[k];
+      }
+      if (p.carry_in) {  // the state entering the shard
+        const float2 ci = __ldg(reinterpret_cast<const float2*>(p.carry_in + (size_t)b * kD + ch0));
+        Y = make_float2(fmaf(Pb, ci.x, Y.x), fmaf(Pb, ci.y, Y.y));
+      }
       const float Pn = c == 0 ? 1.f : p.P[n];
-      const float2 ci = __ldg(reinterpret_cast<const float2*>(p.carry_in + (size_t)b * kD + ch0));
-      X = make_float2(fmaf(Pn, ci.x, X.x), fmaf(Pn, ci.y, X.y));
+      X = make_float2(fmaf(Pn, Y.x, X.x), fmaf(Pn, Y.y, X.y));
     }
   }
   const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
@@ -370,13 +418,16 @@ cudaError_t launch_out(const Params& p, const float* lam_tok, cudaStream_t st) {
 
 using namespace ossm;
 
-// Workspace of the three-pass path: header, decay products, prefix products,
-// aggregates, carries and (gated) the per-token decays.
+// Workspace of the three-pass path: header, chunk decay products, prefix
+// products, aggregates and carries, the same four per carry block, and
+// (gated) the per-token decays.
 size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a) {
   const size_t nch = (size_t)(a->S + p3::kL - 1) / p3::kL;
   const size_t N = (size_t)a->B * p3::kH * nch;
+  const size_t NB = (size_t)a->B * p3::kH * ((nch + p3::kBlk - 1) / p3::kBlk);
   auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
-  size_t bytes = al(sizeof(WsHeader)) + 2 * al(N * 4) + 2 * al(N * p3::kHD * 4);
+  size_t bytes = al(sizeof(WsHeader)) + 2 * al(N * 4) + 2 * al(N * p3::kHD * 4) + 2 * al(NB * 4) +
+                 2 * al(NB * p3::kHD * 4);
   if (a->gate_w && !a->lam_tok) bytes += al((size_t)a->B * a->S * p3::kH * 4);
   return bytes;
 }
@@ -419,12 +470,22 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
   off += al(N * kHD * 4);
   p.carry = reinterpret_cast<float*>(ws + off);
   off += al(N * kHD * 4);
+  p.nblk = (p.nchunks + kBlk - 1) / kBlk;
+  const size_t NB = (size_t)a->B * kH * p.nblk;
+  p.blk_A = reinterpret_cast<float*>(ws + off);
+  off += al(NB * 4);
+  p.blk_P = reinterpret_cast<float*>(ws + off);
+  off += al(NB * 4);
+  p.blk_E = reinterpret_cast<float*>(ws + off);
+  off += al(NB * kHD * 4);
+  p.blk_X = reinterpret_cast<float*>(ws + off);
+  off += al(NB * kHD * 4);
   p.lam_ws = gate ? reinterpret_cast<float*>(ws + off) : nullptr;
   p.starts_seq = 1;
   p.tot_A = nullptr;
   p.tot_E = nullptr;
   p.carry_in = nullptr;
-  if ((long long)a->B * p.nchunks > 0x7fffffffLL) return OSSM_EINVAL;
+  if ((long long)a->B * p.nchunks > 0x7fffffffLL || (long long)a->B * kH * p.nblk > 0x7fffffffLL) return OSSM_EINVAL;
   return OSSM_OK;
 }
 
@@ -441,7 +502,8 @@ int p3_front(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
   else
     e = gate ? launch_agg<true, false>(mx, p, st) : launch_agg<false, false>(mx, p, st);
   if (e != cudaSuccess) return OSSM_ELAUNCH;
-  p3_carry_kernel<<<a->B * kH, kSpans * 32, 0, st>>>(p);
+  p3_carry_kernel<<<a->B * kH * p.nblk, kSpans * 32, 0, st>>>(p);
+  if (p.nblk > 1) p3_blockfold_kernel<<<a->B * kH, 32, 0, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
 }
 

@@ -105,10 +105,12 @@ def _cfg2_like(B, S, D=512, H=8, seed=10):
     return x, c, W, b, init
 
 
-@pytest.mark.parametrize("B,S", [(2, 3000), (1, 16384)])
+@pytest.mark.parametrize("B,S", [(2, 3000), (1, 16384), (1, 40001)])
 def test_bf16_gate_carried_state(B, S):
     """BASELINE configs[1] semantics at reduced size: bf16 I/O, fp32 state,
-    per-token dynamic lambda from Linear(512->8), carried state ~N(0, 0.1)."""
+    per-token dynamic lambda from Linear(512->8), carried state ~N(0, 0.1).
+    S = 40001 gives 1251 chunks per chain: three carry blocks of 512 chunks,
+    the last one and the last chunk ragged."""
     x, c, W, b, init = _cfg2_like(B, S)
     lam = f32(R.BASELINE_LAMBDA)
     out, fin = run(T(x, torch.bfloat16), T(c), lambda_per_head=lam.tolist(), gate_weight=T(W),

@@ -37,7 +37,7 @@ def _problem(B, S, seed):
 
 
 @pytest.mark.parametrize("B,S,G,gate", [(2, 4096, 2, True), (1, 3000, 4, True), (2, 2048, 4, False),
-                                        (1, 40000, 8, True)])
+                                        (1, 40000, 8, True), (1, 70001, 2, True)])
 def test_shards_on_one_gpu_match_unsharded(B, S, G, gate):
     import orthossm_b200 as O
     from orthossm_b200.sdpc_kernel import _fwd_args, fold_shard_carries
