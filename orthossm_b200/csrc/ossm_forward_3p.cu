@@ -51,8 +51,11 @@ constexpr int kHD = 64;  // channels per head
 constexpr int kD = kH * kHD;
 constexpr int kBox = kL * 128;       // one head's [32 x 128 B] box
 constexpr int kTile = kH * kBox;     // 32 KB
-constexpr int kOffPart = kTile;                       // [8 warps][32 tokens][8] f32
-constexpr int kOffLam = kOffPart + kH * kL * kH * 4;  // [8 heads][32] float2 (l, 1 - l)
+// partial gate logits: [8 warps][8 gate outputs][32 tokens + 4] f32; the pad
+// puts the mma fragment writes and the per-token reads in 32 distinct banks
+constexpr int kPartRow = kL + 4;
+constexpr int kOffPart = kTile;
+constexpr int kOffLam = kOffPart + kH * kH * kPartRow * 4;  // [8 heads][32] float2 (l, 1 - l)
 constexpr int kOffBar = kOffLam + kH * kL * 8;
 constexpr int kAggSmem = kOffBar + 16 + 1024;        // + alignment slack
 constexpr int kSpans = 32;                           // carry kernel: warps per block
@@ -155,7 +158,7 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
   if (GATE) {  // this head's 64-channel partial logits for all 8 heads, then the sum
     const uint32_t xa = smem_u32(xs);
     const int m = lane >> 3, rr = lane & 7, gid = lane >> 2, tig = lane & 3;
-    float* pw = part_s + h * (kL * kH);
+    float* pw = part_s + h * (kH * kPartRow);
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
       float d[4] = {0.f, 0.f, 0.f, 0.f};
@@ -167,15 +170,16 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
         mma_bf16_16816(d, a, whi[ks][0], whi[ks][1]);
         mma_bf16_16816(d, a, wlo[ks][0], wlo[ks][1]);
       }
-      pw[(mt * 16 + gid) * kH + 2 * tig] = d[0];
-      pw[(mt * 16 + gid) * kH + 2 * tig + 1] = d[1];
-      pw[(mt * 16 + gid + 8) * kH + 2 * tig] = d[2];
-      pw[(mt * 16 + gid + 8) * kH + 2 * tig + 1] = d[3];
+      // d: tokens mt*16 + gid (+8), gate outputs 2*tig (+1)
+      pw[(2 * tig) * kPartRow + mt * 16 + gid] = d[0];
+      pw[(2 * tig + 1) * kPartRow + mt * 16 + gid] = d[1];
+      pw[(2 * tig) * kPartRow + mt * 16 + gid + 8] = d[2];
+      pw[(2 * tig + 1) * kPartRow + mt * 16 + gid + 8] = d[3];
     }
     __syncthreads();
     float logit = bias_h;
 #pragma unroll
-    for (int g = 0; g < kH; ++g) logit += part_s[g * (kL * kH) + lane * kH + h];
+    for (int g = 0; g < kH; ++g) logit += part_s[(g * kH + h) * kPartRow + lane];
     const float sg = 1.0f / (1.0f + __expf(-logit));
     lam = fminf(fmaxf(lam_base + p.gate_scale * (sg - 0.5f), p.gate_lo), p.gate_hi);
     if (tg < p.S) p.lam_ws[((size_t)b * p.S + tg) * kH + h] = lam;  // for the output pass
