@@ -335,8 +335,10 @@ def run_ours(args):
     out_pin = torch.empty(B, S, D, dtype=torch.bfloat16).pin_memory()
     fin_pin = torch.empty(B, D).pin_memory()
     e2e_steps = max(3, min(K_eff, 20))
-    def e2e_step():  # the public host-buffer call: copies in, forward, copies out, overlapped in parts
-        O.cheby_ema_forward_host(x_pin, c, lambda_per_head=lam, gate_weight=W, gate_bias=bvec, init_state=init,
+    init_pin = init.cpu().pin_memory()  # the carried state comes from the host too
+
+    def e2e_step():  # the public host-buffer call (ossm_cheby_ema_fwd_host): copies in, forward, copies out
+        O.cheby_ema_forward_host(x_pin, c, lambda_per_head=lam, gate_weight=W, gate_bias=bvec, init_state=init_pin,
                                  out_host=out_pin, final_host=fin_pin)
 
     with torch.cuda.stream(stream):
@@ -377,7 +379,7 @@ def run_ours(args):
                          "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                          "peak_kind": peak_kind, "bytes_per_step": scan_bytes,
                          "avg_step_ms": scan_avg},
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": elem * 2,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": elem * 2 + B * D * 4,
                     "d2h_bytes_per_step": elem * 2 + B * D * 4},
             "clocks": clocks,
             "device_status": status,

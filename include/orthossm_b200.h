@@ -126,6 +126,32 @@ int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_t workspace
 #define OSSM_NOALLOC_SCRATCH_BYTES (16u << 20)
 int ossm_cheby_ema_fwd_noalloc(const ossm_fwd_args* a, ossm_stream_t stream, void** scratch);
 
+/* ossm_cheby_ema_fwd on a batch in HOST memory: a->x, a->out, a->init_state
+ * and a->final_state are host pointers (x and out contiguous [B,S,D]; pinned
+ * memory for the copies to overlap, pageable memory works but serialises);
+ * a->coeffs, a->lam_h, a->gate_w, a->gate_b, a->lam_tok and a->lut are device
+ * pointers as for ossm_cheby_ema_fwd; a->tanh_out must be NULL.  The batch
+ * goes through the GPU in about `pieces` parts (groups of whole sequences, or
+ * token ranges of every sequence with the EMA state carried across them):
+ * the copy in of one part, the forward of the next and the copy out of the
+ * one before overlap on side streams that the library keeps per device.  The
+ * caller's stream waits for all of it, so host reads of out / final_state
+ * are valid once that stream's work is done.  Whole-sequence parts give
+ * bitwise the forward of the whole batch; token-range parts differ from it
+ * only in the rounding of the carried state.  The workspace is device memory
+ * of ossm_fwd_host_workspace_bytes(a, pieces), zero-filled once, reused by
+ * host calls ordered on one stream; it holds staging buffers, so it must not
+ * be shared with the other entry points (their workspaces keep launch state
+ * between calls).  Its first 256 bytes are the forward's header, which
+ * ossm_workspace_status reads.  Calls on one device are enqueued one at a
+ * time (a lock); stream capture is not supported.
+ * The reference has no host-buffer call: its callers move tensors to the
+ * GPU themselves before the kernel launch (sdpc_kernel.py:988-1209 with
+ * precision_tests.py:60-72); this entry point is that move, overlapped. */
+size_t ossm_fwd_host_workspace_bytes(const ossm_fwd_args* a, int pieces);
+int ossm_cheby_ema_fwd_host(const ossm_fwd_args* a, int pieces, void* workspace, size_t workspace_bytes,
+                            ossm_stream_t stream);
+
 /* The per-token decay of the gate alone: lam_tok[b,t,h] (f32, [B,S,H]) from
  * a->x, a->gate_w, a->gate_b, a->lam_h, a->gate_scale/lo/hi.  Feeding the
  * result back through a->lam_tok gives the same output as the gated call.

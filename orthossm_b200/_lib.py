@@ -23,6 +23,7 @@ OSSM_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 EXPORTED = (
     "ossm_fwd_workspace_bytes", "ossm_cheby_ema_fwd", "ossm_cheby_ema_fwd_noalloc", "ossm_gate_decay",
+    "ossm_fwd_host_workspace_bytes", "ossm_cheby_ema_fwd_host",
     "ossm_workspace_status", "ossm_fwd_shard_aggregate", "ossm_fwd_shard_output",
     "ossm_cheby_rkv_lion", "ossm_version", "ossm_status_string",
     "ossm_sizeof_fwd_args", "ossm_sizeof_lion_args", "ossm_sizeof_ttt_args",
@@ -93,6 +94,10 @@ def _declare(lib):
     lib.ossm_cheby_ema_fwd.argtypes = [C.POINTER(FwdArgs), _vp, C.c_size_t, _vp]
     lib.ossm_cheby_ema_fwd_noalloc.restype = C.c_int
     lib.ossm_cheby_ema_fwd_noalloc.argtypes = [C.POINTER(FwdArgs), _vp, C.POINTER(_vp)]
+    lib.ossm_fwd_host_workspace_bytes.restype = C.c_size_t
+    lib.ossm_fwd_host_workspace_bytes.argtypes = [C.POINTER(FwdArgs), C.c_int]
+    lib.ossm_cheby_ema_fwd_host.restype = C.c_int
+    lib.ossm_cheby_ema_fwd_host.argtypes = [C.POINTER(FwdArgs), C.c_int, _vp, C.c_size_t, _vp]
     lib.ossm_fwd_shard_aggregate.restype = C.c_int
     lib.ossm_fwd_shard_aggregate.argtypes = [C.POINTER(FwdArgs), C.c_int, _vp, C.c_size_t, _vp, _vp, _vp]
     lib.ossm_fwd_shard_output.restype = C.c_int

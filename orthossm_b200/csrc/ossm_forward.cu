@@ -213,6 +213,10 @@ __global__ void __launch_bounds__(kNT, 2) fwd_scan_kernel(const FwdParams p) {
   __syncthreads();
   const uint32_t ticket = s_ticket;
   const uint32_t epoch = s_epoch;
+  if (ticket >= p.nctas) {  // the header was not left by a launch of this kernel: report it, touch nothing
+    if (tid == 0) atomicExch(&p.ws->status, (uint32_t)OSSM_EWORKSPACE);
+    return;
+  }
   const int BH = p.B * p.H;
   const int c = (int)(ticket / BH);
   const int rem = (int)(ticket % BH);

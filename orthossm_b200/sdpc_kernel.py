@@ -106,17 +106,19 @@ def init_chebyshev_coefficients(batch, n_heads, degree, head_dim, device):
 # ----------------------------------------------------------------------------
 
 _WS: dict = {}
+_WS_HOST: dict = {}  # host-buffer calls: staging buffers inside, never shared with the others
 _WS_LOCK = threading.Lock()
 
 
-def _workspace(device, stream, nbytes):
+def _workspace(device, stream, nbytes, host=False):
     key = (device, stream.cuda_stream)
+    cache = _WS_HOST if host else _WS
     with _WS_LOCK:
-        ws = _WS.get(key)
+        ws = cache.get(key)
         if ws is None or ws.numel() < nbytes:
             # zero-filled once: ticket / epoch / flags start at 0
             ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
-            _WS[key] = ws
+            cache[key] = ws
     return ws
 
 
@@ -125,7 +127,7 @@ def workspace_status(device=None, clear=True):
     3 = a look-back wait timed out).  Synchronises each workspace's stream."""
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     worst = 0
-    for (d, sptr), ws in list(_WS.items()):
+    for (d, sptr), ws in list(_WS.items()) + list(_WS_HOST.items()):
         if d != device:
             continue
         st = L._i32(0)
@@ -157,19 +159,26 @@ def _rowmajor(x):
 def _fwd_args(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None, gate_bias=None,
               gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None, out_dtype=None, return_tanh=False,
               eval_mode="clenshaw", fast_path_semantics=False, precise=None, out=None, final_state=None,
-              lam_tok=None, force_generic=False, extra_flags=0):
+              lam_tok=None, force_generic=False, extra_flags=0, host=False, device=None):
     """ossm_fwd_args for a forward call; returns (args, tensors to keep alive,
-    out, final_state).  extra_flags: further OSSM_F_* kernel selections."""
-    _need_cuda(x, coeffs)
-    x = _rowmajor(x)
-    if x.dtype not in _DT:
-        x = x.float()
+    out, final_state).  extra_flags: further OSSM_F_* kernel selections.
+    host: x, out, init_state and final_state are host tensors (given, for
+    ``out`` and ``final_state``), every other tensor lives on ``device``."""
+    if host:
+        _need_cuda(coeffs)
+        if x.is_cuda or not x.is_contiguous() or x.dtype not in _DT:
+            raise ValueError("host forward: x must be a contiguous bf16 or fp32 host tensor")
+    else:
+        _need_cuda(x, coeffs)
+        x = _rowmajor(x)
+        if x.dtype not in _DT:
+            x = x.float()
     B, S, D = x.shape
     coeffs = coeffs.contiguous().float()
     H, K, hd = coeffs.shape[1], coeffs.shape[2], coeffs.shape[3]
     if H * hd != D or coeffs.shape[0] != B:
         raise ValueError(f"coeffs {tuple(coeffs.shape)} do not match x {tuple(x.shape)}")
-    dev = x.device
+    dev = torch.device(device) if host else x.device
     odt = out_dtype or x.dtype
     if out is None:
         out = torch.empty(B, S, D, device=dev, dtype=odt)
@@ -184,7 +193,7 @@ def _fwd_args(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=
         if lam is None:
             lam = torch.full((H,), float(ema_momentum), device=dev)
     if init_state is not None:
-        init_state = init_state.to(dev, torch.float32).contiguous()
+        init_state = init_state.to(torch.device("cpu") if host else dev, torch.float32).contiguous()
     if lam_tok is not None:
         _need_cuda(lam_tok)
         lam_tok = lam_tok.float().contiguous()
@@ -426,35 +435,34 @@ def cheby_ema_forward_seqpar(x, coeffs, *, group=None, lambda_per_head=None, ema
 # host-resident batches: copies overlapped with the forward
 # ----------------------------------------------------------------------------
 
-_HOST_STREAMS: dict = {}
-
-
-def _side_streams(dev):
-    with _WS_LOCK:
-        st = _HOST_STREAMS.get(dev)
-        if st is None:
-            st = _HOST_STREAMS[dev] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev))
-    return st
-
 
 def cheby_ema_forward_host(x_host, coeffs, *, out_host=None, final_host=None, device=None, pieces=8, **kw):
-    """``cheby_ema_forward`` of a batch that lives in pinned host memory.
+    """``cheby_ema_forward`` of a batch that lives in pinned host memory,
+    through the library's host-buffer entry point ``ossm_cheby_ema_fwd_host``.
 
-    The batch goes through the GPU in ``pieces`` parts: groups of whole
-    sequences when there are at least two, else consecutive token ranges of
-    the one sequence (its EMA state carried from part to part).  Every host
-    slice is contiguous.  Three streams overlap the host-to-device copy of
-    part k+1, the forward of part k and the device-to-host copy of part k-1,
-    on two device buffers per direction; a PCIe link moves both directions at
-    once.  The current stream waits for all of it, so a later host read after
-    a synchronisation (or an event on the current stream) sees the results.
+    The batch goes through the GPU in about ``pieces`` parts: groups of whole
+    sequences when there are at least ``pieces`` sequences, else every
+    sequence cut into consecutive token ranges (its EMA state carried from
+    range to range).  The library overlaps the host-to-device copy of part
+    k+1, the forward of part k and the device-to-host copy of part k-1 on its
+    own side streams; a PCIe link moves both directions at once, and only
+    the first part's copy in and the last part's copy out are not overlapped.
+    Eight parts measured best on B200 over PCIe (each copy has a fixed cost,
+    so smaller parts lose more than they save at the pipeline's ends).  The
+    current stream waits for all of it, so a later host read after a
+    synchronisation (or an event on the current stream) sees the results.
 
-    x_host: pinned CPU tensor [B, S, D] (bf16 or fp32); coeffs and the other
-    keyword arguments as for ``cheby_ema_forward`` (device tensors, or small
-    CPU ones, moved once).  Returns (out_host [B, S, D] in x's dtype unless
-    ``out_dtype`` says otherwise, final_host [B, D] fp32), both pinned."""
+    x_host: pinned CPU tensor [B, S, D] (bf16 or fp32), contiguous;
+    ``init_state`` is read from the host (a device or pageable one is first
+    copied to pinned memory); coeffs and the other keyword arguments as for
+    ``cheby_ema_forward`` (device tensors, or small CPU ones, moved once; a
+    per-token ``lam_tok`` [B, S, H] stays on the device and is cut with the
+    parts).  Returns (out_host [B, S, D] in x's dtype unless ``out_dtype``
+    says otherwise, final_host [B, D] fp32), both pinned."""
     if x_host.is_cuda or not x_host.is_pinned():
         raise ValueError("cheby_ema_forward_host: x_host must be a pinned CPU tensor")
+    if kw.get("return_tanh"):
+        raise NotImplementedError("cheby_ema_forward_host: return_tanh is not supported")
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     B, S, D = x_host.shape
     odt = kw.pop("out_dtype", None) or x_host.dtype
@@ -462,61 +470,25 @@ def cheby_ema_forward_host(x_host, coeffs, *, out_host=None, final_host=None, de
         out_host = torch.empty(B, S, D, dtype=odt).pin_memory()
     if final_host is None:
         final_host = torch.empty(B, D, dtype=torch.float32).pin_memory()
+    if out_host.is_cuda or not out_host.is_pinned() or not out_host.is_contiguous():
+        raise ValueError("cheby_ema_forward_host: out_host must be a contiguous pinned CPU tensor")
+    init = kw.pop("init_state", None)
+    if init is not None and (init.is_cuda or not init.is_pinned() or init.dtype != torch.float32):
+        init = init.detach().to("cpu", torch.float32).contiguous().pin_memory()
     mv = lambda t: t.to(dev, non_blocking=True) if isinstance(t, torch.Tensor) and not t.is_cuda else t  # noqa: E731
     coeffs = mv(coeffs)
     kw = {k: mv(v) for k, v in kw.items()}
-    init = kw.pop("init_state", None)
-    by_batch = B >= 2
-    n = max(1, min(int(pieces), B if by_batch else S))
-    cuts = [(B if by_batch else S) * i // n for i in range(n + 1)]
-    cur = torch.cuda.current_stream(dev)
-    s_in, s_cmp, s_out = _side_streams(dev)
-    big = max(b - a for a, b in zip(cuts[:-1], cuts[1:]))
-    shape = (big, S, D) if by_batch else (1, big, D)
-    xin = [torch.empty(shape, dtype=x_host.dtype, device=dev) for _ in range(2)]
-    yout = [torch.empty(shape, dtype=odt, device=dev) for _ in range(2)]
-    fin = [torch.empty((big if by_batch else 1), D, dtype=torch.float32, device=dev) for _ in range(2)]
-    ev_in = [torch.cuda.Event() for _ in range(n)]
-    ev_cmp = [torch.cuda.Event() for _ in range(n)]
-    ev_out = [torch.cuda.Event() for _ in range(n)]
-    start = torch.cuda.Event()
-    start.record(cur)
-    for s_ in (s_in, s_cmp, s_out):
-        s_.wait_event(start)  # buffers, coefficients and init are ready on the current stream
-    for k in range(n):
-        i = k & 1
-        a, b = cuts[k], cuts[k + 1]
-        m = b - a
-        xh = x_host[a:b] if by_batch else x_host[:, a:b]
-        with torch.cuda.stream(s_in):
-            if k >= 2:
-                s_in.wait_event(ev_cmp[k - 2])  # buffer i was read by the forward of part k-2
-            xd = xin[i][:m] if by_batch else xin[i][:, :m]
-            xd.copy_(xh, non_blocking=True)
-            ev_in[k].record(s_in)
-        with torch.cuda.stream(s_cmp):
-            s_cmp.wait_event(ev_in[k])
-            if k >= 2:
-                s_cmp.wait_event(ev_out[k - 2])  # output buffer i was copied out after part k-2
-            yd = yout[i][:m] if by_batch else yout[i][:, :m]
-            if by_batch:
-                st_in = None if init is None else init[a:b]
-                cheby_ema_forward(xd, coeffs[a:b], init_state=st_in, out=yd, final_state=fin[i][:m],
-                                  out_dtype=odt, **kw)
-            else:
-                st_in = init if k == 0 else fin[i ^ 1]
-                cheby_ema_forward(xd, coeffs, init_state=st_in, out=yd, final_state=fin[i], out_dtype=odt, **kw)
-            ev_cmp[k].record(s_cmp)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(ev_cmp[k])
-            (out_host[a:b] if by_batch else out_host[:, a:b]).copy_(yd, non_blocking=True)
-            if by_batch:
-                final_host[a:b].copy_(fin[i][:m], non_blocking=True)
-            elif k == n - 1:
-                final_host.copy_(fin[i], non_blocking=True)
-            ev_out[k].record(s_out)
-    cur.wait_event(ev_out[n - 1])
-    cur.wait_event(ev_cmp[n - 1])
+    with torch.cuda.device(dev):
+        a, keep, _, _ = _fwd_args(x_host, coeffs, init_state=init, out=out_host, final_state=final_host,
+                                  out_dtype=odt, host=True, device=dev, **kw)
+        lib = L.lib()
+        nbytes = lib.ossm_fwd_host_workspace_bytes(L.C.byref(a), int(pieces))
+        if nbytes == 0:
+            L.check(L.OSSM_EINVAL, "cheby_ema_forward_host (argument check)")
+        stream = torch.cuda.current_stream(dev)
+        ws = _workspace(dev, stream, nbytes, host=True)
+        L.check(lib.ossm_cheby_ema_fwd_host(L.C.byref(a), int(pieces), ws.data_ptr(), ws.numel(), stream.cuda_stream),
+                "cheby_ema_forward_host")
     return out_host, final_host
 
 

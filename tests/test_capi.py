@@ -87,3 +87,24 @@ def test_ops_refuse_cpu_tensors():
     from orthossm_b200 import cheby_ema_forward
     with pytest.raises(RuntimeError, match="CUDA"):
         cheby_ema_forward(torch.zeros(1, 8, 64), torch.zeros(1, 8, 8, 8))
+
+
+def test_host_workspace_size_and_validation():
+    """ossm_fwd_host_workspace_bytes: the device forward's workspace for the
+    largest part plus the part plan's staging buffers; no GPU needed."""
+    lib = L.lib()
+    B, S = 8, 4096
+    base = dict(B=B, S=S, x_stride_b=S * 512, out_stride_b=S * 512)
+    n8 = lib.ossm_fwd_host_workspace_bytes(C.byref(_args(**base)), 8)
+    n16 = lib.ossm_fwd_host_workspace_bytes(C.byref(_args(**base)), 16)
+    one_part = S * 512 * 2  # one sequence of bf16 activations
+    assert n8 % 256 == 0 and n8 >= 2 * 2 * one_part  # two x and two out buffers of one sequence each
+    assert n16 < n8  # 16 parts: half sequences
+    assert lib.ossm_fwd_host_workspace_bytes(C.byref(_args(**base)), 1) >= 2 * 2 * B * one_part
+    bad = [(_args(**base), 0), (_args(**dict(base, x_stride_b=S * 512 + 512)), 8),
+           (_args(**dict(base, out_stride_s=1024)), 8), (_args(**dict(base, tanh_out=4096)), 8),
+           (_args(**dict(base, degree=9)), 8)]
+    for a, pieces in bad:
+        assert lib.ossm_fwd_host_workspace_bytes(C.byref(a), pieces) == 0
+    assert lib.ossm_cheby_ema_fwd_host(C.byref(_args(**base)), 8, None, 0, None) == L.OSSM_EWORKSPACE
+    assert lib.ossm_cheby_ema_fwd_host(C.byref(_args(**dict(base, tanh_out=4096))), 8, None, 0, None) == L.OSSM_EINVAL
