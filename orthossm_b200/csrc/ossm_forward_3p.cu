@@ -345,7 +345,7 @@ OSSM_DEV float2 out_chunk_general(const __nv_bfloat16* xp, OT* op, long long xs,
 }
 
 template <bool PRECISE, typename OT, bool CONTIG>
-__global__ void __launch_bounds__(kNT, 3) p3_out_kernel(const Params p, const float* lam_tok) {
+__global__ void __launch_bounds__(kNT, PRECISE ? 3 : 4) p3_out_kernel(const Params p, const float* lam_tok) {
   __shared__ float2 lam_s[kH * kL];
   const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
   const int j0 = lane * 2, ch0 = h * kHD + j0;
