@@ -30,6 +30,9 @@
 // reference's semantics (u = 0 there).
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <mutex>
+
 #include "ossm_eval.cuh"
 
 // shared with the single-pass path (ossm_forward_tc.cu)
@@ -425,14 +428,57 @@ using namespace ossm;
 // Workspace of the three-pass path: header, chunk decay products, prefix
 // products, aggregates and carries, the same four per carry block, and
 // (gated) the per-token decays.
-size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a) {
+namespace {
+
+size_t p3_al(size_t v) { return (v + 255) & ~(size_t)255; }
+
+size_t p3_single_bytes(const ossm_fwd_args* a) {
   const size_t nch = (size_t)(a->S + p3::kL - 1) / p3::kL;
   const size_t N = (size_t)a->B * p3::kH * nch;
   const size_t NB = (size_t)a->B * p3::kH * ((nch + p3::kBlk - 1) / p3::kBlk);
-  auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
-  size_t bytes = al(sizeof(WsHeader)) + 2 * al(N * 4) + 2 * al(N * p3::kHD * 4) + 2 * al(NB * 4) +
-                 2 * al(NB * p3::kHD * 4);
-  if (a->gate_w && !a->lam_tok) bytes += al((size_t)a->B * a->S * p3::kH * 4);
+  size_t bytes = p3_al(sizeof(WsHeader)) + 2 * p3_al(N * 4) + 2 * p3_al(N * p3::kHD * 4) + 2 * p3_al(NB * 4) +
+                 2 * p3_al(NB * p3::kHD * 4);
+  if (a->gate_w && !a->lam_tok) bytes += p3_al((size_t)a->B * a->S * p3::kH * 4);
+  return bytes;
+}
+
+// A batch runs as kGroups groups of whole sequences on kStreams streams when
+// every group still fills the GPU for about two waves of the streaming
+// kernels (ossm_p3_launch), else as one launch.
+constexpr int kGroups = 2, kStreams = 2;
+int p3_groups(const ossm_fwd_args* a) {
+  const long long nch = (a->S + p3::kL - 1) / p3::kL;
+  return (a->B >= kGroups && (long long)(a->B / kGroups) * nch >= 1024) ? kGroups : 1;
+}
+
+// Sequences [b0, b1) of a batch: the same arguments, pointers moved to row b0.
+ossm_fwd_args p3_rows(const ossm_fwd_args* a, int b0, int b1) {
+  ossm_fwd_args h = *a;
+  const size_t D = (size_t)a->H * a->head_dim;
+  const size_t oel = a->out_dtype == OSSM_F32 ? 4 : 2;
+  h.B = b1 - b0;
+  h.x = static_cast<const char*>(a->x) + (size_t)b0 * a->x_stride_b * 2;  // bf16 (the path's only input type)
+  h.out = static_cast<char*>(a->out) + (size_t)b0 * a->out_stride_b * oel;
+  h.coeffs = a->coeffs + (size_t)b0 * a->H * a->degree * a->head_dim;
+  if (a->init_state) h.init_state = a->init_state + (size_t)b0 * D;
+  if (a->final_state) h.final_state = a->final_state + (size_t)b0 * D;
+  if (a->lam_tok) h.lam_tok = a->lam_tok + (size_t)b0 * a->S * a->H;
+  return h;
+}
+
+}  // namespace
+
+size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a) {
+  size_t bytes = p3_single_bytes(a);
+  const int G = p3_groups(a);
+  if (G > 1) {
+    size_t sum = 0;
+    for (int g = 0; g < G; ++g) {
+      const ossm_fwd_args h = p3_rows(a, a->B * g / G, a->B * (g + 1) / G);
+      sum += p3_al(p3_single_bytes(&h));
+    }
+    bytes = std::max(bytes, sum);
+  }
   return bytes;
 }
 
@@ -493,8 +539,8 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
   return OSSM_OK;
 }
 
-// passes 1 and 2: aggregates, carries (and the shard totals when asked)
-int p3_front(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
+// pass 1: aggregates
+int p3_aggregates(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
   using namespace p3;
   CUtensorMap mx;
   if (!fast::encode_map(&mx, a->x, a->S, a->B, a->x_stride_s, a->x_stride_b)) return OSSM_EINVAL;
@@ -505,10 +551,21 @@ int p3_front(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
     e = gate ? launch_agg<true, true>(mx, p, st) : launch_agg<false, true>(mx, p, st);
   else
     e = gate ? launch_agg<true, false>(mx, p, st) : launch_agg<false, false>(mx, p, st);
-  if (e != cudaSuccess) return OSSM_ELAUNCH;
+  return e == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
+}
+
+// pass 2: carries (and the shard totals when asked)
+int p3_carries(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
+  using namespace p3;
   p3_carry_kernel<<<a->B * kH * p.nblk, kSpans * 32, 0, st>>>(p);
   if (p.nblk > 1) p3_blockfold_kernel<<<a->B * kH, 32, 0, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
+}
+
+// passes 1 and 2
+int p3_front(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
+  const int r = p3_aggregates(a, p, st);
+  return r != OSSM_OK ? r : p3_carries(a, p, st);
 }
 
 // pass 3: outputs
@@ -525,9 +582,69 @@ int p3_back(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
   return e == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
 }
 
+// The side streams of a split launch and their events, one set per device,
+// created by the first split launch on the device (make that call before any
+// stream capture); a mutex keeps each launch's enqueue in one piece.
+struct P3Side {
+  std::mutex mu;
+  bool ready = false;
+  cudaStream_t s[kStreams] = {};
+  cudaEvent_t fork = nullptr, join[kStreams] = {};
+};
+P3Side g_p3side[64];
+
+// Groups of whole sequences, group g on stream g % kStreams (stream 0 is the
+// caller's), all forked at once.  The block scheduler dispatches the first
+// group's aggregate CTAs first, so its aggregates finish while the others'
+// still run, and the carry pass of each group (a few dozen CTAs that would
+// leave most SMs idle between the streaming passes) overlaps other groups'
+// streaming work.  The groups use disjoint parts of one workspace and report
+// to its header.  Every result is bitwise the one-launch result.
+int p3_launch_split(const ossm_fwd_args* a, int G, char* ws, cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return OSSM_ELAUNCH;
+  P3Side& sd = g_p3side[dev];
+  std::lock_guard<std::mutex> lock(sd.mu);
+  if (!sd.ready) {
+    for (int k = 1; k < kStreams; ++k)
+      if (cudaStreamCreateWithFlags(&sd.s[k], cudaStreamNonBlocking) != cudaSuccess) return OSSM_ELAUNCH;
+    if (cudaEventCreateWithFlags(&sd.fork, cudaEventDisableTiming) != cudaSuccess) return OSSM_ELAUNCH;
+    for (int k = 1; k < kStreams; ++k)
+      if (cudaEventCreateWithFlags(&sd.join[k], cudaEventDisableTiming) != cudaSuccess) return OSSM_ELAUNCH;
+    sd.ready = true;
+  }
+  cudaStream_t streams[kStreams];
+  streams[0] = st;
+  for (int k = 1; k < kStreams; ++k) streams[k] = sd.s[k];
+  bool ok = cudaEventRecord(sd.fork, st) == cudaSuccess;
+  for (int k = 1; k < kStreams; ++k) ok = ok && cudaStreamWaitEvent(sd.s[k], sd.fork, 0) == cudaSuccess;
+  int r = ok ? OSSM_OK : OSSM_ELAUNCH;
+  WsHeader* header = reinterpret_cast<WsHeader*>(ws);
+  size_t off = 0;
+  for (int g = 0; g < G && r == OSSM_OK; ++g) {
+    const ossm_fwd_args h = p3_rows(a, a->B * g / G, a->B * (g + 1) / G);
+    p3::Params p;
+    r = p3_params(&h, ws + off, p);
+    off += p3_al(p3_single_bytes(&h));
+    if (r != OSSM_OK) break;
+    p.ws = header;  // one header: the sticky status lives at the workspace start
+    r = p3_front(&h, p, streams[g % kStreams]);
+    if (r == OSSM_OK) r = p3_back(&h, p, streams[g % kStreams]);
+  }
+  // join, also after an error, so the caller's later work never overlaps
+  bool joined = true;
+  for (int k = 1; k < kStreams; ++k)
+    joined = joined && cudaEventRecord(sd.join[k], sd.s[k]) == cudaSuccess &&
+             cudaStreamWaitEvent(st, sd.join[k], 0) == cudaSuccess;
+  if (r != OSSM_OK) return r;
+  return joined ? OSSM_OK : OSSM_ELAUNCH;
+}
+
 }  // namespace
 
 int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
+  const int G = p3_groups(a);
+  if (G > 1) return p3_launch_split(a, G, ws, st);
   p3::Params p;
   int r = p3_params(a, ws, p);
   if (r != OSSM_OK) return r;

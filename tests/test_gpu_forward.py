@@ -269,3 +269,29 @@ def test_nan_inf_and_huge_inputs(path):
     assert np.isfinite(o).all() and np.isfinite(N(fin)).all()
     assert relerr(o, ref["out"]) < BF16_TOL
     assert relerr(N(fin), ref["final"]) < BF16_TOL
+
+
+@pytest.mark.parametrize("mode", ["gate", "lamtok", "f32out"])
+def test_two_stream_batch_split_is_bitwise_the_per_sequence_result(mode):
+    """B = 4 x S = 16384 runs as two halves on two streams (each half fills a
+    wave of the streaming kernels); every row must be bitwise what a launch
+    of that sequence alone (one stream) gives, carried state included."""
+    B, S = 4, 16384
+    x, c, W, b, init = _cfg2_like(B, S, seed=60)
+    xb, cb, ib = T(x, torch.bfloat16), T(c), T(init)
+    kw = dict(lambda_per_head=R.BASELINE_LAMBDA.tolist() if hasattr(R.BASELINE_LAMBDA, "tolist")
+              else list(R.BASELINE_LAMBDA))
+    lt = None
+    if mode == "gate":
+        kw.update(gate_weight=T(W), gate_bias=T(b))
+    if mode == "lamtok":
+        lt = (0.99 + 0.01 * torch.rand(B, S, 8, generator=torch.Generator().manual_seed(3))).to(dev)
+    odt = torch.float32 if mode == "f32out" else torch.bfloat16
+    out, fin = run(xb, cb, init_state=ib, out_dtype=odt, lam_tok=lt, **kw)
+    for i in range(B):
+        oi, fi = run(xb[i:i + 1].contiguous(), cb[i:i + 1].contiguous(), init_state=ib[i:i + 1].contiguous(),
+                     out_dtype=odt, lam_tok=None if lt is None else lt[i:i + 1].contiguous(), **kw)
+        assert torch.equal(out[i:i + 1], oi), (mode, i)
+        assert torch.equal(fin[i:i + 1], fi), (mode, i)
+    import orthossm_b200 as O
+    assert O.workspace_status() == 0
