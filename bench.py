@@ -646,7 +646,7 @@ def run_cfg4(args):
         print(json.dumps({
             "metric": "tokens/sec", "value": world * Bl * Sl / (step / 1e3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 compute (bf16 x), fp32 state and GEMMs",
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 compute (bf16 x), fp32 state, W_pred GEMMs on TF32 tensor cores (fp32 accumulate)",
             "data": "synthetic (seeded)",
             "config": {"workload": "cfg4: W_pred MSE TTT with forget-gated Adam, per GPU B=4 x S=32768, "
                                    "2048-token chunks (16 sequential steps), W_pred 512x512",

@@ -186,6 +186,10 @@ __global__ void __launch_bounds__(32) rev_carry_kernel(const Params p) {
   }
 }
 
+// DX: the backward (input gradient, carried-in state gradient); without it
+// (the TTT step) only the coefficient gradient is formed, so T_k', y' and the
+// division for dx are not computed at all.
+template <bool DX>
 __global__ void __launch_bounds__(256) rev_grad_kernel(const Params p) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= p.B * p.H * p.ngrp * p.nq) return;
@@ -246,19 +250,19 @@ __global__ void __launch_bounds__(256) rev_grad_kernel(const Params p) {
 #pragma unroll
         for (int k = 2; k < kMaxK; ++k) {
           T[k] = fmaf(2.f * xn, T[k - 1], -T[k - 2]);
-          dT[k] = fmaf(2.f * xn, dT[k - 1], fmaf(2.f, T[k - 1], -dT[k - 2]));
+          if (DX) dT[k] = fmaf(2.f * xn, dT[k - 1], fmaf(2.f, T[k - 1], -dT[k - 2]));
         }
         float y = 0.f, yp = 0.f;
 #pragma unroll
         for (int k = 0; k < kMaxK; ++k) {
           y = fmaf(cf[e][k], T[k], y);
-          yp = fmaf(cf[e][k], dT[k], yp);
+          if (DX) yp = fmaf(cf[e][k], dT[k], yp);
         }
         const float z = gamma * y;
         const bool live = p.fastpath || fabsf(z) < 4.f;  // the fused clamp passes no gradient where it bites
         const float u = p.fastpath ? tanhf(z) : tanhf(fminf(fmaxf(z, -4.f), 4.f));
         float w = 1.f - at;  // ds_t / du_t
-        if (!p.ttt && t == 0 && !p.fastpath) {  // token 0: the carried-in state and its clamp
+        if (DX && t == 0 && !p.fastpath) {  // token 0: the carried-in state and its clamp
           const float iv = p.init ? p.init[(size_t)b * D + ch] : 0.f;
           const bool pass = fabsf(fmaf(at, iv, (1.f - at) * u)) <= 1.f;
           if (!pass) w = 0.f;
@@ -268,14 +272,16 @@ __global__ void __launch_bounds__(256) rev_grad_kernel(const Params p) {
         if (p.seg == 0 || t < p.seg)  // segmented: the gradient of segment 0's coefficients
 #pragma unroll
           for (int k = 0; k < kMaxK; ++k) acc[e][k] = fmaf(dy, T[k], acc[e][k]);
-        const float d1 = 1.f + fabsf(x);
-        // dxn/dx = 1/(1+|x|)^2 (the fast path's clamp of |x| at 1e-7 passes nothing below it)
-        if (!nan && !(p.fastpath && fabsf(x) < 1e-7f)) dx = dy * yp / (d1 * d1);
-      } else if (!p.ttt && t == 0 && p.ginit) {  // fused, NaN at token 0: u = 0
+        if (DX) {
+          const float d1 = 1.f + fabsf(x);
+          // dxn/dx = 1/(1+|x|)^2 (the fast path's clamp of |x| at 1e-7 passes nothing below it)
+          if (!nan && !(p.fastpath && fabsf(x) < 1e-7f)) dx = dy * yp / (d1 * d1);
+        }
+      } else if (DX && t == 0 && p.ginit) {  // fused, NaN at token 0: u = 0
         const float iv = p.init ? p.init[(size_t)b * D + ch] : 0.f;
         p.ginit[(size_t)b * D + ch] = fabsf(at * iv) <= 1.f ? at * adj[e] : 0.f;
       }
-      if (!p.ttt) {
+      if (DX) {
         const size_t o = (size_t)b * p.gxsb + (size_t)t * p.gxss + ch;
         if (p.gx_bf16)
           reinterpret_cast<__nv_bfloat16*>(p.gx)[o] = __float2bfloat16_rn(dx);
@@ -337,7 +343,10 @@ int run(Params& p, char* ws, cudaStream_t st) {
   const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
   rev_agg_kernel<<<blocks, 256, 0, st>>>(p);
   rev_carry_kernel<<<(unsigned)(BH * p.ngrp), 32, 0, st>>>(p);
-  rev_grad_kernel<<<blocks, 256, 0, st>>>(p);
+  if (p.ttt)
+    rev_grad_kernel<false><<<blocks, 256, 0, st>>>(p);
+  else
+    rev_grad_kernel<true><<<blocks, 256, 0, st>>>(p);
   const size_t per = BH * p.K * p.HD;
   rev_reduce_kernel<<<(unsigned)((per + 255) / 256), 256, 0, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
