@@ -271,11 +271,11 @@ def run_ours(args):
         step(0)
         step(1)
     torch.cuda.synchronize()
-    # the bf16 head_dim-64 fast path: p3_agg_kernel, p3_carry_kernel, p3_out_kernel,
-    # once per group of sequences; a batch whose halves each hold >= 1024
-    # (sequence, 32-token chunk) units runs as two halves on two streams
+    # the bf16 head_dim-64 fast path: p3_prep_kernel, p3_agg_kernel, p3_carry_kernel,
+    # p3_out_kernel, once per group of sequences; a batch whose halves each hold
+    # >= 1024 (sequence, 32-token chunk) units runs as two halves on two streams
     groups = 2 if B >= 2 and (B // 2) * ((S + 31) // 32) >= 1024 else 1
-    launches_per_step = 3 * groups
+    launches_per_step = 4 * groups
 
     # ---- clocks: sample through a loaded soak and the timed region ----
     try:

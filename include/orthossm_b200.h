@@ -176,7 +176,7 @@ int ossm_gate_decay(const ossm_fwd_args* a, float* lam_tok, ossm_stream_t stream
  *     X_0 = init_state (or 0), X_{q+1} = shard_decay_q * X_q + shard_state_q.
  *  3. ossm_fwd_shard_output: the shard's outputs (and final_state, the state
  *     after its last token) from that carry_in [B*D] (ignored when
- *     starts_sequence). */
+ *     starts_sequence), on the workspace step 1 filled. */
 int ossm_fwd_shard_aggregate(const ossm_fwd_args* a, int starts_sequence, void* workspace, size_t workspace_bytes,
                              float* shard_decay, float* shard_state, ossm_stream_t stream);
 int ossm_fwd_shard_output(const ossm_fwd_args* a, int starts_sequence, const float* carry_in, void* workspace,

@@ -77,6 +77,8 @@ struct Params {
   float gate_scale, gate_lo, gate_hi;
   const float* lam_in;  // caller's per-token decay [B,S,H] or NULL
   float* lam_ws;        // per-token decays written by the gate [B,S,H] (workspace)
+  float4* cmono;        // [B*8][4][32]: each lane's gamma-folded, 4^-k-scaled monomial coefficients
+  uint4* wfrag;         // [8][4][32]: each lane's mma B fragments of the gate weights, bf16 hi + lo
   const float* init;
   float* fin;
   void* out;
@@ -103,6 +105,48 @@ struct Params {
 OSSM_DEV void split_bf16x2(float2 w, uint32_t& hi, uint32_t& lo) {
   hi = pack_bf16x2(w.x, w.y);
   lo = pack_bf16x2(w.x - __uint_as_float(hi << 16), w.y - __uint_as_float(hi & 0xffff0000u));
+}
+
+// The lane's 16 prepared monomial coefficients of head h of sequence b.
+OSSM_DEV void load_mono(const Params& p, int b, int h, int lane, float2 (&m)[8]) {
+  const float4* src = p.cmono + (size_t)(b * kH + h) * 4 * 32 + lane;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 v = __ldg(src + q * 32);
+    m[2 * q] = make_float2(v.x, v.y);
+    m[2 * q + 1] = make_float2(v.z, v.w);
+  }
+}
+
+// The per-CTA setup of the streaming kernels, done once per launch: warp
+// (b, h) converts head h's coefficients of sequence b for the fast path
+// (MONO), and with the gate warp h splits the weight columns of head h into
+// its lanes' mma fragments.  The same arithmetic the kernels did inline, so
+// the results are bitwise those of an inline setup.
+template <bool MONO, bool GATE>
+__global__ void __launch_bounds__(32) p3_prep_kernel(const Params p) {
+  const int lane = threadIdx.x;
+  const int nmono = MONO ? p.B * kH : 0;
+  if ((int)blockIdx.x < nmono) {
+    const int b = blockIdx.x / kH, h = blockIdx.x % kH;
+    const float gamma = 0.98f - 0.06f * (float)h / (float)kH;
+    float2 cm[8];
+    load_coeffs<false>(p.coeffs, p.K, b, h, lane * 2, gamma, cm);
+    float4* dst = p.cmono + (size_t)blockIdx.x * 4 * 32 + lane;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[q * 32] = make_float4(cm[2 * q].x, cm[2 * q].y, cm[2 * q + 1].x, cm[2 * q + 1].y);
+  } else if (GATE) {
+    const int h = blockIdx.x - nmono;
+    const int gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const float* wr = p.gate_w + (size_t)gid * kD + h * kHD + ks * 16 + 2 * tig;
+      uint32_t hi0, lo0, hi1, lo1;
+      split_bf16x2(__ldg(reinterpret_cast<const float2*>(wr)), hi0, lo0);
+      split_bf16x2(__ldg(reinterpret_cast<const float2*>(wr + 8)), hi1, lo1);
+      p.wfrag[(h * 4 + ks) * 32 + lane] = make_uint4(hi0, hi1, lo0, lo1);
+    }
+  }
 }
 
 // Decay of token (t0 + lane), head h, from a per-token input or the constant.
@@ -135,22 +179,25 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
 #pragma unroll
     for (int hh = 0; hh < kH; ++hh) tma_load_3d(sm + hh * kBox, &tmap_x, bar, hh * kHD, t0, b);
   }
-  // while the tile lands: coefficients, gate weights, the caller's decay
+  // while the tile lands: coefficients, gate weights (both prepared by
+  // p3_prep_kernel on the fast path), the caller's decay
   float2 cm[8];
-  load_coeffs<PRECISE>(p.coeffs, p.K, b, h, j0, gamma, cm);
+  if (PRECISE)
+    load_coeffs<true>(p.coeffs, p.K, b, h, j0, gamma, cm);
+  else
+    load_mono(p, b, h, lane, cm);
   const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
   float lam = GATE ? lam_base : lam_token(p, p.lam_in, b, tg, h, lam_base);
   uint32_t whi[4][2], wlo[4][2];  // mma B fragments of W[gid][h*64 + ks*16 + ...], split bf16 hi + lo
   float bias_h = 0.f;
   if (GATE) {
-    const int gid = lane >> 2, tig = lane & 3;
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
-      const float* wr = p.gate_w + (size_t)gid * kD + h * kHD + ks * 16 + 2 * tig;
-      const float2 w01 = __ldg(reinterpret_cast<const float2*>(wr));
-      const float2 w89 = __ldg(reinterpret_cast<const float2*>(wr + 8));
-      split_bf16x2(w01, whi[ks][0], wlo[ks][0]);
-      split_bf16x2(w89, whi[ks][1], wlo[ks][1]);
+      const uint4 f = __ldg(p.wfrag + (h * 4 + ks) * 32 + lane);
+      whi[ks][0] = f.x;
+      whi[ks][1] = f.y;
+      wlo[ks][0] = f.z;
+      wlo[ks][1] = f.w;
     }
     bias_h = __ldg(p.gate_b + h);
   }
@@ -384,7 +431,10 @@ __global__ void __launch_bounds__(kNT, PRECISE ? 3 : 4) p3_out_kernel(const Para
   const float lam = lam_token(p, lam_tok, b, t0 + lane, h, lam_base);
   lam_s[h * kL + lane] = make_float2(lam, 1.f - lam);
   float2 cm[8];
-  load_coeffs<PRECISE>(p.coeffs, p.K, b, h, j0, gamma, cm);
+  if (PRECISE)
+    load_coeffs<true>(p.coeffs, p.K, b, h, j0, gamma, cm);
+  else
+    load_mono(p, b, h, lane, cm);
   __syncwarp();
 
   const __nv_bfloat16* xp = p.x + (size_t)b * p.xsb + (size_t)t0 * p.xss + ch0;
@@ -438,6 +488,7 @@ size_t p3_single_bytes(const ossm_fwd_args* a) {
   const size_t NB = (size_t)a->B * p3::kH * ((nch + p3::kBlk - 1) / p3::kBlk);
   size_t bytes = p3_al(sizeof(WsHeader)) + 2 * p3_al(N * 4) + 2 * p3_al(N * p3::kHD * 4) + 2 * p3_al(NB * 4) +
                  2 * p3_al(NB * p3::kHD * 4);
+  bytes += p3_al((size_t)a->B * p3::kH * 4 * 32 * 16) + p3_al((size_t)p3::kH * 4 * 32 * 16);  // cmono, wfrag
   if (a->gate_w && !a->lam_tok) bytes += p3_al((size_t)a->B * a->S * p3::kH * 4);
   return bytes;
 }
@@ -530,6 +581,10 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
   off += al(NB * kHD * 4);
   p.blk_X = reinterpret_cast<float*>(ws + off);
   off += al(NB * kHD * 4);
+  p.cmono = reinterpret_cast<float4*>(ws + off);
+  off += al((size_t)a->B * kH * 4 * 32 * 16);
+  p.wfrag = reinterpret_cast<uint4*>(ws + off);
+  off += al((size_t)kH * 4 * 32 * 16);
   p.lam_ws = gate ? reinterpret_cast<float*>(ws + off) : nullptr;
   p.starts_seq = 1;
   p.tot_A = nullptr;
@@ -546,6 +601,15 @@ int p3_aggregates(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) 
   if (!fast::encode_map(&mx, a->x, a->S, a->B, a->x_stride_s, a->x_stride_b)) return OSSM_EINVAL;
   const bool gate = a->gate_w && !a->lam_tok;
   const bool precise = (a->out_dtype == OSSM_F32) || (a->flags & OSSM_F_PRECISE);
+  const int nprep = (precise ? 0 : a->B * kH) + (gate ? kH : 0);
+  if (nprep > 0) {
+    if (precise)
+      p3_prep_kernel<false, true><<<nprep, 32, 0, st>>>(p);
+    else if (gate)
+      p3_prep_kernel<true, true><<<nprep, 32, 0, st>>>(p);
+    else
+      p3_prep_kernel<true, false><<<nprep, 32, 0, st>>>(p);
+  }
   cudaError_t e;
   if (precise)
     e = gate ? launch_agg<true, true>(mx, p, st) : launch_agg<false, true>(mx, p, st);
