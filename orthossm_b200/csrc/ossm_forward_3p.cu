@@ -367,12 +367,15 @@ __global__ void __launch_bounds__(32) p3_blockfold_kernel(const Params p) {
 // One chunk of one head: x and out with token strides XS / OS (elements;
 // compile-time when the tensors are contiguous, so every access is an
 // immediate offset), all 32 tokens (FULL) or the ragged last chunk.
-template <bool PRECISE, typename OT, typename Stride>
-OSSM_DEV float2 out_chunk(const __nv_bfloat16* xp, OT* op, Stride xs, Stride os, float2 X, const float2* lam, bool first,
-                          const float2 (&cm)[8], float gamma) {
-  uint32_t r[kL];
+template <typename Stride>
+OSSM_DEV void load_chunk(const __nv_bfloat16* xp, Stride xs, uint32_t (&r)[kL]) {
 #pragma unroll
   for (int t = 0; t < kL; ++t) r[t] = __ldcs(reinterpret_cast<const unsigned int*>(xp + t * xs));
+}
+// The chunk from its x words r (already loaded).
+template <bool PRECISE, typename OT, typename Stride>
+OSSM_DEV float2 out_chunk_loaded(const uint32_t (&r)[kL], const __nv_bfloat16* xp, OT* op, Stride xs, Stride os,
+                                 float2 X, const float2* lam, bool first, const float2 (&cm)[8], float gamma) {
   auto raw = [&](int t) { return r[t]; };
   auto emit = [&](int t, float2 v) { st2(op + t * os, sizeof(OT) == 4 ? make_float2(clamp1(v.x), clamp1(v.y)) : v); };
   float2 s = ema_chunk<PRECISE, false>(X, lam, first, cm, gamma, raw, emit);
@@ -381,6 +384,13 @@ OSSM_DEV float2 out_chunk(const __nv_bfloat16* xp, OT* op, Stride xs, Stride os,
     s = ema_chunk_exact<PRECISE>(X, lam, first, cm, gamma, reraw, emit);
   }
   return s;
+}
+template <bool PRECISE, typename OT, typename Stride>
+OSSM_DEV float2 out_chunk(const __nv_bfloat16* xp, OT* op, Stride xs, Stride os, float2 X, const float2* lam, bool first,
+                          const float2 (&cm)[8], float gamma) {
+  uint32_t r[kL];
+  load_chunk(xp, xs, r);
+  return out_chunk_loaded<PRECISE, OT>(r, xp, op, xs, os, X, lam, first, cm, gamma);
 }
 // The ragged last chunk (nt < 32 tokens), or strided tensors: a rolled loop
 // with the reference's semantics throughout.
@@ -403,6 +413,12 @@ __global__ void __launch_bounds__(kNT, PRECISE ? 3 : 4) p3_out_kernel(const Para
   const int t0 = c * kL, nt = min(kL, p.S - t0);
   const float gamma = 0.98f - 0.06f * (float)h / (float)kH;
   const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
+  const __nv_bfloat16* xp = p.x + (size_t)b * p.xsb + (size_t)t0 * p.xss + ch0;
+  OT* op = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + (size_t)t0 * p.oss + ch0;
+  // A full chunk of contiguous x: its loads go out first, so their latency
+  // overlaps the carry, decay and coefficient loads below.
+  uint32_t r[kL];
+  if (CONTIG && nt == kL) load_chunk(xp, kD, r);
 
   const bool first = c == 0 && p.starts_seq;
   float2 X;
@@ -437,13 +453,11 @@ __global__ void __launch_bounds__(kNT, PRECISE ? 3 : 4) p3_out_kernel(const Para
     load_mono(p, b, h, lane, cm);
   __syncwarp();
 
-  const __nv_bfloat16* xp = p.x + (size_t)b * p.xsb + (size_t)t0 * p.xss + ch0;
-  OT* op = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + (size_t)t0 * p.oss + ch0;
   float2 s;
   if (nt < kL)
     s = out_chunk_general<PRECISE, OT>(xp, op, p.xss, p.oss, nt, X, lam_s + h * kL, first, cm, gamma);
   else if (CONTIG)
-    s = out_chunk<PRECISE, OT>(xp, op, kD, kD, X, lam_s + h * kL, first, cm, gamma);
+    s = out_chunk_loaded<PRECISE, OT>(r, xp, op, kD, kD, X, lam_s + h * kL, first, cm, gamma);
   else
     s = out_chunk<PRECISE, OT>(xp, op, p.xss, p.oss, X, lam_s + h * kL, first, cm, gamma);
   // decays are 1 past the end, so the chunk's last state is the sequence's final state
