@@ -2,8 +2,11 @@
  * orthossm_b200 — C ABI of the B200-native Cheby-RKV hot path.
  *
  * Plain pointers and sizes; no torch types.  Every entry point is
- * stream-ordered on the caller's stream, allocates nothing, and returns an
- * ossm_status.  Device pointers are caller-allocated.  Tensors are row-major
+ * stream-ordered on the caller's stream, allocates no device memory, and
+ * returns an ossm_status.  Some spread their work over side streams the
+ * library creates once per device (the bf16 forward of a large batch, the
+ * host-buffer forward); that work is forked from and joined back to the
+ * caller's stream within the call.  Device pointers are caller-allocated.  Tensors are row-major
  * and contiguous along the channel axis; [B,S,D] activations take explicit
  * batch / token strides in elements.
  *
@@ -67,6 +70,10 @@ enum ossm_dtype { OSSM_F32 = 0, OSSM_BF16 = 1 };
  * single-pass kernel whose chunk carries are relayed by dedicated warps
  * (x read once, every element evaluated once).  Same function. */
 #define OSSM_F_RELAY (1u << 6)
+/* Keep all of the call's work on the caller's stream: no side streams, so the
+ * bf16 forward of a large batch does not split into two halves.  Same
+ * function, bitwise. */
+#define OSSM_F_ONE_STREAM (1u << 7)
 
 /* ---------------------------------------------------------------------------
  * Fused softsign -> Chebyshev -> gamma_h damping -> tanh -> lambda-EMA scan.
@@ -122,7 +129,8 @@ int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_t workspace
  * The first call on each GPU sets the array up (device address, a clear on
  * `stream`): make it before other work that could overlap it and before any
  * stream capture.  If `scratch` is not NULL it receives the array's device
- * address, for ossm_workspace_status. */
+ * address, for ossm_workspace_status.  All of its work stays on `stream`
+ * (it runs as if OSSM_F_ONE_STREAM were set). */
 #define OSSM_NOALLOC_SCRATCH_BYTES (16u << 20)
 int ossm_cheby_ema_fwd_noalloc(const ossm_fwd_args* a, ossm_stream_t stream, void** scratch);
 

@@ -19,6 +19,7 @@ OSSM_F_PRECISE = 1 << 3
 OSSM_F_GENERIC = 1 << 4
 OSSM_F_SINGLE_PASS = 1 << 5
 OSSM_F_RELAY = 1 << 6
+OSSM_F_ONE_STREAM = 1 << 7
 OSSM_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 EXPORTED = (

@@ -512,6 +512,7 @@ size_t p3_single_bytes(const ossm_fwd_args* a) {
 // kernels (ossm_p3_launch), else as one launch.
 constexpr int kGroups = 2, kStreams = 2;
 int p3_groups(const ossm_fwd_args* a) {
+  if (a->flags & OSSM_F_ONE_STREAM) return 1;
   const long long nch = (a->S + p3::kL - 1) / p3::kL;
   return (a->B >= kGroups && (long long)(a->B / kGroups) * nch >= 1024) ? kGroups : 1;
 }

@@ -65,5 +65,8 @@ extern "C" int ossm_cheby_ema_fwd_noalloc(const ossm_fwd_args* a, ossm_stream_t 
     ptr = g_scratch_ptr[dev];
   }
   if (scratch) *scratch = ptr;
-  return ossm_cheby_ema_fwd(a, ptr, (size_t)OSSM_NOALLOC_SCRATCH_BYTES, stream);
+  // everything on the caller's stream: no side streams are created or used
+  ossm_fwd_args one = *a;
+  one.flags |= OSSM_F_ONE_STREAM;
+  return ossm_cheby_ema_fwd(&one, ptr, (size_t)OSSM_NOALLOC_SCRATCH_BYTES, stream);
 }

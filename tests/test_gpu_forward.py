@@ -288,6 +288,11 @@ def test_two_stream_batch_split_is_bitwise_the_per_sequence_result(mode):
         lt = (0.99 + 0.01 * torch.rand(B, S, 8, generator=torch.Generator().manual_seed(3))).to(dev)
     odt = torch.float32 if mode == "f32out" else torch.bfloat16
     out, fin = run(xb, cb, init_state=ib, out_dtype=odt, lam_tok=lt, **kw)
+    # the same launch kept on the caller's stream (OSSM_F_ONE_STREAM)
+    from orthossm_b200 import _lib as L
+    from orthossm_b200.sdpc_kernel import _cheby_ema_forward
+    o1, f1 = _cheby_ema_forward(xb, cb, init_state=ib, out_dtype=odt, lam_tok=lt, extra_flags=L.OSSM_F_ONE_STREAM, **kw)
+    assert torch.equal(out, o1) and torch.equal(fin, f1), mode
     for i in range(B):
         oi, fi = run(xb[i:i + 1].contiguous(), cb[i:i + 1].contiguous(), init_state=ib[i:i + 1].contiguous(),
                      out_dtype=odt, lam_tok=None if lt is None else lt[i:i + 1].contiguous(), **kw)
