@@ -378,7 +378,7 @@ def run_ours(args):
                        "l2": "inputs larger than L2: two rotating 134 MB input buffers"},
             "gpu_launches": launches_per_step * K_eff,
             "hbm_gbs_step": (elem * 4 + B * D * 8) / (ms / K_eff / 1e3) / 1e9,
-            "roofline": {"bound": "hbm", "kernel": "forward step: p3_agg_kernel (gate + chunk aggregates) + p3_carry_kernel + p3_out_kernel", "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": "forward step: p3_prep_kernel + p3_agg_kernel (gate + chunk aggregates) + p3_carry_kernel + p3_out_kernel" + (", two halves of the batch on two streams" if groups == 2 else ""), "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                          "peak_kind": peak_kind, "bytes_per_step": scan_bytes,
                          "avg_step_ms": scan_avg},
