@@ -558,9 +558,13 @@ def ttt_wpred_adam(x, coeffs, m, v, step, W_pred, *, lambda_per_head=None, ema_m
                                    out_dtype=torch.float32, out=out[:, t0:t0 + Lc])
         gs = None
         if Lc > 1:
+            # one elementwise launch subtracts the bf16 next tokens in fp32 (no
+            # separate conversion); the 2/N scale rides in the second GEMM's alpha
             with _matmul_precision(gemm):
-                r = torch.matmul(s[:, :-1], Wp.t()) - xc[:, 1:].float()
-                gs = torch.matmul(r, Wp).mul_(2.0 / ((Lc - 1) * D)).contiguous()
+                r = torch.matmul(s[:, :-1], Wp.t())
+                r.sub_(xc[:, 1:])
+                r2 = r.view(-1, D)
+                gs = torch.addmm(r2, r2, Wp, beta=0.0, alpha=2.0 / ((Lc - 1) * D)).view(B, Lc - 1, D)
         step += 1
         a = L.TttArgs(B=B, L=Lc, H=H, head_dim=hd, degree=K, x=xc.data_ptr(), x_dtype=_DT[xdt],
                       x_stride_b=xc.stride(0), x_stride_s=xc.stride(1), coeffs=c.data_ptr(), m=m.data_ptr(),
