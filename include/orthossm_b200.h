@@ -71,8 +71,10 @@ enum ossm_dtype { OSSM_F32 = 0, OSSM_BF16 = 1 };
  * (x read once, every element evaluated once).  Same function. */
 #define OSSM_F_RELAY (1u << 6)
 /* Keep all of the call's work on the caller's stream: no side streams, so the
- * bf16 forward of a large batch does not split into two halves.  Same
- * function, bitwise. */
+ * bf16 forward of a large batch does not split into two halves (same results,
+ * bitwise) and one long sequence (at least 4096 chunks of 32 tokens) does not
+ * split into two token ranges (same results up to the fp32 rounding of the
+ * carried state). */
 #define OSSM_F_ONE_STREAM (1u << 7)
 
 /* ---------------------------------------------------------------------------

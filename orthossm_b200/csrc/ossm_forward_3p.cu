@@ -532,6 +532,29 @@ ossm_fwd_args p3_rows(const ossm_fwd_args* a, int b0, int b1) {
   return h;
 }
 
+// One long sequence (B = 1, at least 4096 chunks) runs as two consecutive
+// token ranges on two streams (ossm_p3_launch).
+bool p3_seq_split(const ossm_fwd_args* a) {
+  if (a->flags & OSSM_F_ONE_STREAM) return false;
+  const long long nch = (a->S + p3::kL - 1) / p3::kL;
+  return a->B == 1 && nch >= 4096;
+}
+int p3_seq_cut(const ossm_fwd_args* a) { return ((a->S + p3::kL - 1) / p3::kL / 2) * p3::kL; }
+
+// Tokens [s0, s1) of a one-sequence batch: the initial state belongs to the
+// range that starts the sequence, the final state to the one that ends it.
+ossm_fwd_args p3_tokens(const ossm_fwd_args* a, int s0, int s1) {
+  ossm_fwd_args h = *a;
+  const size_t oel = a->out_dtype == OSSM_F32 ? 4 : 2;
+  h.S = s1 - s0;
+  h.x = static_cast<const char*>(a->x) + (size_t)s0 * a->x_stride_s * 2;  // bf16
+  h.out = static_cast<char*>(a->out) + (size_t)s0 * a->out_stride_s * oel;
+  if (a->lam_tok) h.lam_tok = a->lam_tok + (size_t)s0 * a->H;
+  if (s0 > 0) h.init_state = nullptr;
+  if (s1 < a->S) h.final_state = nullptr;
+  return h;
+}
+
 }  // namespace
 
 size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a) {
@@ -544,6 +567,12 @@ size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a) {
       sum += p3_al(p3_single_bytes(&h));
     }
     bytes = std::max(bytes, sum);
+  }
+  if (p3_seq_split(a)) {  // both ranges, then the first range's totals
+    const int cut = p3_seq_cut(a);
+    const ossm_fwd_args h0 = p3_tokens(a, 0, cut), h1 = p3_tokens(a, cut, a->S);
+    bytes = std::max(bytes, p3_al(p3_single_bytes(&h0)) + p3_al(p3_single_bytes(&h1)) +
+                                p3_al((size_t)a->B * p3::kH * 4) + p3_al((size_t)a->B * p3::kD * 4));
   }
   return bytes;
 }
@@ -668,9 +697,22 @@ struct P3Side {
   std::mutex mu;
   bool ready = false;
   cudaStream_t s[kStreams] = {};
-  cudaEvent_t fork = nullptr, join[kStreams] = {};
+  cudaEvent_t fork = nullptr, join[kStreams] = {}, tot = nullptr;
 };
 P3Side g_p3side[64];
+
+// The device's side streams and events, created on first use (caller holds mu).
+bool p3_side_ready(P3Side& sd) {
+  if (sd.ready) return true;
+  for (int k = 1; k < kStreams; ++k)
+    if (cudaStreamCreateWithFlags(&sd.s[k], cudaStreamNonBlocking) != cudaSuccess) return false;
+  if (cudaEventCreateWithFlags(&sd.fork, cudaEventDisableTiming) != cudaSuccess) return false;
+  if (cudaEventCreateWithFlags(&sd.tot, cudaEventDisableTiming) != cudaSuccess) return false;
+  for (int k = 1; k < kStreams; ++k)
+    if (cudaEventCreateWithFlags(&sd.join[k], cudaEventDisableTiming) != cudaSuccess) return false;
+  sd.ready = true;
+  return true;
+}
 
 // Groups of whole sequences, group g on stream g % kStreams (stream 0 is the
 // caller's), all forked at once.  The block scheduler dispatches the first
@@ -684,14 +726,7 @@ int p3_launch_split(const ossm_fwd_args* a, int G, char* ws, cudaStream_t st) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return OSSM_ELAUNCH;
   P3Side& sd = g_p3side[dev];
   std::lock_guard<std::mutex> lock(sd.mu);
-  if (!sd.ready) {
-    for (int k = 1; k < kStreams; ++k)
-      if (cudaStreamCreateWithFlags(&sd.s[k], cudaStreamNonBlocking) != cudaSuccess) return OSSM_ELAUNCH;
-    if (cudaEventCreateWithFlags(&sd.fork, cudaEventDisableTiming) != cudaSuccess) return OSSM_ELAUNCH;
-    for (int k = 1; k < kStreams; ++k)
-      if (cudaEventCreateWithFlags(&sd.join[k], cudaEventDisableTiming) != cudaSuccess) return OSSM_ELAUNCH;
-    sd.ready = true;
-  }
+  if (!p3_side_ready(sd)) return OSSM_ELAUNCH;
   cudaStream_t streams[kStreams];
   streams[0] = st;
   for (int k = 1; k < kStreams; ++k) streams[k] = sd.s[k];
@@ -719,11 +754,54 @@ int p3_launch_split(const ossm_fwd_args* a, int G, char* ws, cudaStream_t st) {
   return joined ? OSSM_OK : OSSM_ELAUNCH;
 }
 
+// One long sequence as two token ranges, range 0 on the caller's stream and
+// range 1 on the side stream, forked at once.  Each range's aggregates and
+// carries need nothing from the other, so the carry pass of each overlaps
+// the other's streaming kernels.  Range 0 also writes its totals (the state
+// at its end), and range 1's output pass waits for them and adds them as the
+// state entering it, exactly as a sequence-sharded launch on two ranks does.
+// The carries compose in another order than in one launch, so results match
+// the one-launch results to fp32 rounding of the carries, not bitwise.
+int p3_launch_seq_split(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return OSSM_ELAUNCH;
+  P3Side& sd = g_p3side[dev];
+  std::lock_guard<std::mutex> lock(sd.mu);
+  if (!p3_side_ready(sd)) return OSSM_ELAUNCH;
+  const int cut = p3_seq_cut(a);
+  const ossm_fwd_args h0 = p3_tokens(a, 0, cut), h1 = p3_tokens(a, cut, a->S);
+  const size_t off1 = p3_al(p3_single_bytes(&h0)), off_tot = off1 + p3_al(p3_single_bytes(&h1));
+  float* tot_A = reinterpret_cast<float*>(ws + off_tot);
+  float* tot_E = reinterpret_cast<float*>(ws + off_tot + p3_al((size_t)a->B * p3::kH * 4));
+  p3::Params p0, p1;
+  int r = p3_params(&h0, ws, p0);
+  if (r == OSSM_OK) r = p3_params(&h1, ws + off1, p1);
+  if (r != OSSM_OK) return r;
+  p0.tot_A = tot_A;
+  p0.tot_E = tot_E;
+  p1.ws = p0.ws;  // one header: the sticky status lives at the workspace start
+  p1.starts_seq = 0;
+  p1.carry_in = tot_E;
+  cudaStream_t side = sd.s[1];
+  bool ok = cudaEventRecord(sd.fork, st) == cudaSuccess && cudaStreamWaitEvent(side, sd.fork, 0) == cudaSuccess;
+  r = ok ? p3_front(&h0, p0, st) : OSSM_ELAUNCH;
+  ok = r == OSSM_OK && cudaEventRecord(sd.tot, st) == cudaSuccess;
+  if (ok) r = p3_back(&h0, p0, st);
+  if (ok && r == OSSM_OK) r = p3_front(&h1, p1, side);
+  if (ok && r == OSSM_OK) ok = cudaStreamWaitEvent(side, sd.tot, 0) == cudaSuccess;
+  if (ok && r == OSSM_OK) r = p3_back(&h1, p1, side);
+  // join, also after an error, so the caller's later work never overlaps
+  const bool joined = cudaEventRecord(sd.join[1], side) == cudaSuccess && cudaStreamWaitEvent(st, sd.join[1], 0) == cudaSuccess;
+  if (r != OSSM_OK) return r;
+  return ok && joined ? OSSM_OK : OSSM_ELAUNCH;
+}
+
 }  // namespace
 
 int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
   const int G = p3_groups(a);
   if (G > 1) return p3_launch_split(a, G, ws, st);
+  if (p3_seq_split(a)) return p3_launch_seq_split(a, ws, st);
   p3::Params p;
   int r = p3_params(a, ws, p);
   if (r != OSSM_OK) return r;

@@ -300,3 +300,32 @@ def test_two_stream_batch_split_is_bitwise_the_per_sequence_result(mode):
         assert torch.equal(fin[i:i + 1], fi), (mode, i)
     import orthossm_b200 as O
     assert O.workspace_status() == 0
+
+
+@pytest.mark.parametrize("gate", [True, False])
+def test_long_single_sequence_runs_as_two_ranges(gate):
+    """B = 1 x S = 131849 (4121 chunks) runs as two token ranges on two
+    streams, the second taking the first's end state as its carry-in.  The
+    one-stream launch (OSSM_F_ONE_STREAM; oracle-checked at smaller sizes)
+    is the reference: outputs within bf16 shard tolerance, the final state to
+    fp32 rounding of the carries, and the first four 512-chunk blocks (whose
+    carries fold identically in both) bitwise."""
+    import orthossm_b200 as O
+    from orthossm_b200 import _lib as L
+    from orthossm_b200.sdpc_kernel import _cheby_ema_forward
+    S = 4096 * 32 + 777
+    g = torch.Generator().manual_seed(81)
+    x = torch.randn(1, S, 512, generator=g).to(torch.bfloat16).to(dev)
+    c = (torch.randn(1, 8, 8, 64, generator=g) / torch.arange(1, 9).view(1, 1, 8, 1)).to(dev)
+    init = (0.1 * torch.randn(1, 512, generator=g)).to(dev)
+    kw = dict(lambda_per_head=list(R.BASELINE_LAMBDA), init_state=init)
+    if gate:
+        kw.update(gate_weight=((torch.rand(8, 512, generator=g) * 2 - 1) / 512 ** 0.5).to(dev),
+                  gate_bias=((torch.rand(8, generator=g) * 2 - 1) / 512 ** 0.5).to(dev))
+    out, fin = run(x, c, **kw)
+    o1, f1 = _cheby_ema_forward(x, c, extra_flags=L.OSSM_F_ONE_STREAM, **kw)
+    assert (out.float() - o1.float()).abs().max().item() <= 2 ** -7
+    assert relerr(N(fin), N(f1)) < 1e-5
+    head = 4 * 512 * 32
+    assert torch.equal(out[:, :head], o1[:, :head])
+    assert O.workspace_status() == 0
