@@ -583,6 +583,17 @@ def run_cfg3(args):
         fn = lambda: O.cheby_ema_forward_seqpar(x, c, lambda_per_head=lam, out=out)  # noqa: E731
     else:
         fn = lambda: O.cheby_ema_forward(x, c, lambda_per_head=lam, out=out)  # noqa: E731
+    if args.profile_once:  # 3 warm-up calls + the profiled one, nothing timed
+        sampler.stop()
+        with torch.cuda.stream(stream):
+            for _ in range(4):
+                fn()
+        torch.cuda.synchronize()
+        if rank == 0:
+            print("profile-once done, status", O.workspace_status())
+        if world > 1:
+            dist.destroy_process_group()
+        return
     t_end = time.perf_counter() + args.soak_s
     with torch.cuda.stream(stream):
         while time.perf_counter() < t_end:
