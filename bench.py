@@ -45,6 +45,13 @@ WORKLOAD = ("cfg2: per GPU B=8 x S=16384 tokens, D=512 (8 heads x 64), Chebyshev
             "bf16 in/out, fp32 state, per-token decay gate Linear(512->8), carried state N(0,0.1)")
 
 
+def config_dict(world):
+    """The workload description both arms print, so their lines compare."""
+    return {"workload": WORKLOAD, "global_batch": B * world, "seq_len": S,
+            "parallelism": f"batch-sharded x{world} (no collective)",
+            "l2": "inputs larger than L2: two rotating 134 MB input buffers"}
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -149,7 +156,7 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 compute (bf16 in/out)", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": S, "parallelism": "host cores"},
+        "config": config_dict(int(os.environ.get("WORLD_SIZE", "1"))),
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": nth, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -361,6 +368,9 @@ def run_ours(args):
     e2e_value = world * B * S * e2e_steps / (e2e_ms / 1e3)
     status = O.workspace_status()
 
+    # ---- BASELINE configs[2] sharded over the ranks (the sequence-parallel design) ----
+    seqpar = seqpar_record(args, world, rank, dev, stream, barrier, max_over_ranks)
+
     # ---- CPU baseline on rank 0 at N=1 ----
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -373,9 +383,7 @@ def run_ours(args):
             "steps": K_eff, "warmup": max(args.warmup, 3), "ms_per_step": ms / K_eff,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 compute (bf16 in/out)", "data": "synthetic (seeded, BASELINE.json configs[1] shapes)",
-            "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": S,
-                       "parallelism": f"batch-sharded x{world} (no collective)",
-                       "l2": "inputs larger than L2: two rotating 134 MB input buffers"},
+            "config": config_dict(world),
             "gpu_launches": launches_per_step * K_eff,
             "hbm_gbs_step": (elem * 4 + B * D * 8) / (ms / K_eff / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "forward step: p3_prep_kernel + p3_agg_kernel (gate + chunk aggregates) + p3_carry_kernel + p3_out_kernel" + (", two halves of the batch on two streams" if groups == 2 else ""), "achieved": achieved, "peak": peak,
@@ -389,10 +397,59 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        line["seqpar"] = seqpar
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
         dist.destroy_process_group()
+
+
+def seqpar_record(args, world, rank, dev, stream, barrier, max_over_ranks):
+    """BASELINE.json configs[2] on the same ranks: one sequence of 1,048,576
+    tokens (bf16, per-head decays, no gate, zero initial state) sharded along
+    the sequence, rank r holding tokens [r S/N, (r+1) S/N).  Each step is the
+    shard's aggregate pass, one NCCL all-gather of the packed shard totals,
+    the device fold and the shard's output pass (at N = 1, the unsharded
+    forward).  Timed with CUDA events, max over ranks; strong scaling (the
+    total work is fixed).  parity_ok compares every rank's outputs with the
+    unsharded single-GPU forward of the whole sequence (to one bf16 step) and
+    the final state with its final state (1e-4 relative)."""
+    import torch
+    import torch.distributed as dist
+    import orthossm_b200 as O
+    S_all = 1 << 20
+    Sl = S_all // world
+    g = torch.Generator(device=dev).manual_seed(99)
+    x = torch.randn(1, S_all, D, generator=g, device=dev).to(torch.bfloat16)
+    c = (torch.randn(1, H, K, HD, generator=g, device=dev) / torch.arange(1, K + 1, device=dev).view(1, 1, K, 1))
+    lam = torch.tensor(LAMBDA, device=dev)
+    xs = x[:, rank * Sl:(rank + 1) * Sl].contiguous()
+    out = torch.empty_like(xs)
+    if world > 1:
+        fn = lambda: O.cheby_ema_forward_seqpar(xs, c, lambda_per_head=lam, out=out)  # noqa: E731
+    else:
+        fn = lambda: O.cheby_ema_forward(xs, c, lambda_per_head=lam, out=out)  # noqa: E731
+    steps = max(3, min(args.steps, 20))
+    ms = _timed(fn, steps, args.warmup, stream, barrier, max_over_ranks)
+    with torch.cuda.stream(stream):
+        _, fin = fn()
+        full, fin_full = O.cheby_ema_forward(x, c, lambda_per_head=lam)
+    torch.cuda.synchronize()
+    err = (out.float() - full[:, rank * Sl:(rank + 1) * Sl].float()).abs().max().item()
+    ferr = ((fin - fin_full).norm() / fin_full.norm()).item()
+    err, ferr = max_over_ranks(err), max_over_ranks(ferr)
+    step_ms = ms / steps
+    peak, kind = peaks()
+    gbs = S_all * D * 4 / world / (step_ms / 1e3) / 1e9
+    del x, full
+    return {"workload": "cfg3: one sequence of 1,048,576 tokens, D=512, degree 8, bf16 in/out, per-head decays, "
+                        "no gate, sequence-sharded over the ranks", "n_gpus": world, "scaling": "strong",
+            "tokens_per_s": S_all / (step_ms / 1e3), "ms_per_sequence": step_ms, "steps": steps,
+            "parallelism": ("sequence-sharded x%d: shard aggregates, one NCCL all-gather of the packed shard "
+                            "totals, device fold, shard outputs" % world) if world > 1 else "one GPU, unsharded",
+            "hbm_gbs_per_gpu": gbs, "hbm_frac_per_gpu": gbs / peak, "peak_kind": kind,
+            "parity_ok": bool(err <= 2 ** -7 and ferr < 1e-4), "max_abs_err_vs_unsharded": err,
+            "final_state_relerr_vs_unsharded": ferr, "device_status": O.workspace_status()}
 
 
 def run_lm(args):

@@ -62,14 +62,6 @@ enum ossm_dtype { OSSM_F32 = 0, OSSM_BF16 = 1 };
 /* Use the generic forward kernel even where the TMA / tcgen05 path applies
  * (the two paths compute the same function; used to test one against the other). */
 #define OSSM_F_GENERIC (1u << 4)
-/* On the bf16 fast path (bf16 x, 8 heads of 64), use the single-pass kernel
- * (chunk look-back across CTAs) instead of the default three-pass one
- * (chunk aggregates, carry scan, outputs).  Same function; kept for comparison. */
-#define OSSM_F_SINGLE_PASS (1u << 5)
-/* On the bf16 fast path with bf16 output and 4 to 32 sequences, use the
- * single-pass kernel whose chunk carries are relayed by dedicated warps
- * (x read once, every element evaluated once).  Same function. */
-#define OSSM_F_RELAY (1u << 6)
 /* Keep all of the call's work on the caller's stream: no side streams, so the
  * bf16 forward of a large batch does not split into two halves (same results,
  * bitwise) and one long sequence (at least 4096 chunks of 32 tokens) does not
@@ -180,17 +172,27 @@ int ossm_gate_decay(const ossm_fwd_args* a, float* lam_tok, ossm_stream_t stream
  *  1. ossm_fwd_shard_aggregate: chunk aggregates and carries of the shard from
  *     a zero state (from a->init_state on the shard that starts the sequence),
  *     and the shard's totals: shard_decay[b*H + h] = the product of the decays
- *     over the shard, shard_state[b*D + d] = the state at its end.
- *  2. The caller exchanges the totals (an all-gather of (B*H + B*D) floats per
- *     rank) and folds the state entering its shard:
- *     X_0 = init_state (or 0), X_{q+1} = shard_decay_q * X_q + shard_state_q.
- *  3. ossm_fwd_shard_output: the shard's outputs (and final_state, the state
- *     after its last token) from that carry_in [B*D] (ignored when
- *     starts_sequence), on the workspace step 1 filled. */
+ *     over the shard, shard_state[b*D + d] = the state at its end.  With
+ *     shard_state = shard_decay + B*H the totals form one packed record of
+ *     B*H + B*D floats, so one all-gather moves them.
+ *  2. The caller all-gathers the packed records into totals
+ *     [nshards][B*H + B*D] (rank order).
+ *  3. ossm_fwd_shard_output: folds, on the device and in shard order, the
+ *     state entering shard `shard` from totals[0 .. shard) and seq_init (the
+ *     state before token 0 of the sequence, or NULL for zeros):
+ *     X_0 = seq_init, X_{q+1} = shard_decay_q * X_q + shard_state_q; then
+ *     writes the shard's outputs (and final_state, the state after its last
+ *     token) on the workspace step 1 filled.  Shard 0 starts from
+ *     a->init_state and reads no totals.
+ *  ossm_fwd_shard_fold writes the state after the first `nshards` shards
+ *  ([B*D], the same fold; nshards = all shards gives the sequence's final
+ *  state on every rank). */
 int ossm_fwd_shard_aggregate(const ossm_fwd_args* a, int starts_sequence, void* workspace, size_t workspace_bytes,
                              float* shard_decay, float* shard_state, ossm_stream_t stream);
-int ossm_fwd_shard_output(const ossm_fwd_args* a, int starts_sequence, const float* carry_in, void* workspace,
-                          size_t workspace_bytes, ossm_stream_t stream);
+int ossm_fwd_shard_output(const ossm_fwd_args* a, int shard, const float* totals, const float* seq_init,
+                          void* workspace, size_t workspace_bytes, ossm_stream_t stream);
+int ossm_fwd_shard_fold(int32_t B, int32_t H, int32_t head_dim, int32_t nshards, const float* totals,
+                        const float* seq_init, float* state_out, ossm_stream_t stream);
 
 /* Read (and optionally clear) the sticky device status word of a workspace:
  * OSSM_OK, or OSSM_ETIMEOUT if a look-back wait gave up.  Synchronises the

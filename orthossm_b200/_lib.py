@@ -17,15 +17,13 @@ OSSM_EVAL_CLENSHAW, OSSM_EVAL_LUT, OSSM_EVAL_CLENSHAW_DEG4 = 0, 1, 2
 OSSM_F_FASTPATH = 1 << 2
 OSSM_F_PRECISE = 1 << 3
 OSSM_F_GENERIC = 1 << 4
-OSSM_F_SINGLE_PASS = 1 << 5
-OSSM_F_RELAY = 1 << 6
 OSSM_F_ONE_STREAM = 1 << 7
 OSSM_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 EXPORTED = (
     "ossm_fwd_workspace_bytes", "ossm_cheby_ema_fwd", "ossm_cheby_ema_fwd_noalloc", "ossm_gate_decay",
     "ossm_fwd_host_workspace_bytes", "ossm_cheby_ema_fwd_host",
-    "ossm_workspace_status", "ossm_fwd_shard_aggregate", "ossm_fwd_shard_output",
+    "ossm_workspace_status", "ossm_fwd_shard_aggregate", "ossm_fwd_shard_output", "ossm_fwd_shard_fold",
     "ossm_cheby_rkv_lion", "ossm_version", "ossm_status_string",
     "ossm_sizeof_fwd_args", "ossm_sizeof_lion_args", "ossm_sizeof_ttt_args",
     "ossm_ttt_workspace_bytes", "ossm_ttt_wpred_step", "ossm_sizeof_bwd_args", "ossm_bwd_workspace_bytes",
@@ -102,7 +100,9 @@ def _declare(lib):
     lib.ossm_fwd_shard_aggregate.restype = C.c_int
     lib.ossm_fwd_shard_aggregate.argtypes = [C.POINTER(FwdArgs), C.c_int, _vp, C.c_size_t, _vp, _vp, _vp]
     lib.ossm_fwd_shard_output.restype = C.c_int
-    lib.ossm_fwd_shard_output.argtypes = [C.POINTER(FwdArgs), C.c_int, _vp, _vp, C.c_size_t, _vp]
+    lib.ossm_fwd_shard_output.argtypes = [C.POINTER(FwdArgs), C.c_int, _vp, _vp, _vp, C.c_size_t, _vp]
+    lib.ossm_fwd_shard_fold.restype = C.c_int
+    lib.ossm_fwd_shard_fold.argtypes = [C.c_int32, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp, _vp]
     lib.ossm_gate_decay.restype = C.c_int
     lib.ossm_gate_decay.argtypes = [C.POINTER(FwdArgs), _vp, _vp]
     lib.ossm_workspace_status.restype = C.c_int

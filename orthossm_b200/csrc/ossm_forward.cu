@@ -418,17 +418,15 @@ __global__ void __launch_bounds__(kNT, 2) fwd_scan_kernel(const FwdParams p) {
 // ---------------------------------------------------------------------------
 using namespace ossm;
 
-bool ossm_tc_eligible(const ossm_fwd_args* a);
-size_t ossm_tc_workspace_bytes(const ossm_fwd_args* a);
-int ossm_tc_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
+bool ossm_p3_eligible(const ossm_fwd_args* a);
 size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a);
-bool ossm_sp_eligible(const ossm_fwd_args* a);
-size_t ossm_sp_workspace_bytes(const ossm_fwd_args* a);
-int ossm_sp_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
 int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
 int ossm_p3_shard_front(const ossm_fwd_args* a, int starts_sequence, char* ws, float* shard_decay, float* shard_state,
                         cudaStream_t st);
-int ossm_p3_shard_back(const ossm_fwd_args* a, int starts_sequence, const float* carry_in, char* ws, cudaStream_t st);
+int ossm_p3_shard_back(const ossm_fwd_args* a, int shard, const float* totals, const float* seq_init, char* ws,
+                       cudaStream_t st);
+int ossm_p3_shard_fold(int B, int H, int hd, int nshards, const float* totals, const float* init, float* state_out,
+                       cudaStream_t st);
 
 namespace {
 
@@ -495,10 +493,7 @@ FwdLayout fwd_layout(const ossm_fwd_args* a) {
   l.off_lam = off;
   if (a->gate_w && !a->lam_tok) off = align256(off + (size_t)a->B * a->S * a->H * 4);
   l.total = off;
-  if (ossm_tc_eligible(a))  // bf16 fast paths: whichever layout the flags select
-    l.total = (a->flags & OSSM_F_SINGLE_PASS) ? ossm_tc_workspace_bytes(a)
-              : ((a->flags & OSSM_F_RELAY) && ossm_sp_eligible(a)) ? ossm_sp_workspace_bytes(a)
-                                                                  : ossm_p3_workspace_bytes(a);
+  if (ossm_p3_eligible(a)) l.total = ossm_p3_workspace_bytes(a);  // the bf16 fast path
   return l;
 }
 
@@ -548,6 +543,20 @@ extern "C" size_t ossm_fwd_workspace_bytes(const ossm_fwd_args* a) {
   return fwd_layout(a).total;
 }
 
+// Library-internal: where the generic kernel's look-back flags sit in the
+// workspace of these arguments ([offset, offset + bytes)), or 0 bytes when
+// the call takes the bf16 fast path, which keeps no flags between launches.
+// A workspace shared by calls of different shapes must have this region
+// cleared before each generic launch: the flags of one shape can lie over
+// another shape's aggregates, and a stale float with a flag's bit pattern
+// would pass as a published record.
+size_t ossm_fwd_flag_region(const ossm_fwd_args* a, size_t* offset) {
+  if (validate_fwd(a) != OSSM_OK || ossm_p3_eligible(a)) return 0;
+  const FwdLayout l = fwd_layout(a);
+  if (offset) *offset = l.off_flag;
+  return l.N * 4;
+}
+
 extern "C" int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_t workspace_bytes,
                                   ossm_stream_t stream) {
   const int v = validate_fwd(a);
@@ -591,11 +600,7 @@ extern "C" int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_
   p.incB = reinterpret_cast<float*>(ws + l.off_incB);
   p.nctas = (uint32_t)l.N;
 
-  if (ossm_tc_eligible(a)) {
-    if (a->flags & OSSM_F_SINGLE_PASS) return ossm_tc_launch(a, ws, st);
-    if ((a->flags & OSSM_F_RELAY) && ossm_sp_eligible(a)) return ossm_sp_launch(a, ws, st);
-    return ossm_p3_launch(a, ws, st);
-  }
+  if (ossm_p3_eligible(a)) return ossm_p3_launch(a, ws, st);
 
   if (a->gate_w && !a->lam_tok) {
     if (launch_gate(a, reinterpret_cast<float*>(ws + l.off_lam), st) != cudaSuccess) return OSSM_ELAUNCH;
@@ -620,7 +625,7 @@ namespace {
 int shard_check(const ossm_fwd_args* a, void* workspace, size_t workspace_bytes) {
   const int v = validate_fwd(a);
   if (v != OSSM_OK) return v;
-  if (!ossm_tc_eligible(a) || (a->flags & OSSM_F_SINGLE_PASS)) return OSSM_EINVAL;
+  if (!ossm_p3_eligible(a)) return OSSM_EINVAL;
   if (!workspace || workspace_bytes < ossm_p3_workspace_bytes(a) || ((uintptr_t)workspace % 256))
     return OSSM_EWORKSPACE;
   return OSSM_OK;
@@ -637,12 +642,21 @@ extern "C" int ossm_fwd_shard_aggregate(const ossm_fwd_args* a, int starts_seque
                              reinterpret_cast<cudaStream_t>(stream));
 }
 
-extern "C" int ossm_fwd_shard_output(const ossm_fwd_args* a, int starts_sequence, const float* carry_in,
+extern "C" int ossm_fwd_shard_output(const ossm_fwd_args* a, int shard, const float* totals, const float* seq_init,
                                      void* workspace, size_t workspace_bytes, ossm_stream_t stream) {
   const int v = shard_check(a, workspace, workspace_bytes);
   if (v != OSSM_OK) return v;
-  if (!starts_sequence && (!carry_in || ((uintptr_t)carry_in % 8))) return OSSM_EINVAL;
-  return ossm_p3_shard_back(a, starts_sequence, carry_in, static_cast<char*>(workspace),
+  if (shard < 0 || (shard > 0 && (!totals || ((uintptr_t)totals % 4)))) return OSSM_EINVAL;
+  if (seq_init && ((uintptr_t)seq_init % 4)) return OSSM_EINVAL;
+  return ossm_p3_shard_back(a, shard, totals, seq_init, static_cast<char*>(workspace),
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ossm_fwd_shard_fold(int32_t B, int32_t H, int32_t head_dim, int32_t nshards, const float* totals,
+                                   const float* seq_init, float* state_out, ossm_stream_t stream) {
+  if (B < 1 || H < 1 || head_dim < 1 || nshards < 0 || !state_out || (nshards > 0 && !totals)) return OSSM_EINVAL;
+  if ((long long)B * H * head_dim > 0x7fffffffLL) return OSSM_EINVAL;
+  return ossm_p3_shard_fold(B, H, head_dim, nshards, totals, seq_init, state_out,
                             reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -35,13 +35,56 @@
 
 #include "ossm_eval.cuh"
 
-// shared with the single-pass path (ossm_forward_tc.cu)
 namespace ossm {
 namespace fast {
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
-bool encode_map(CUtensorMap* map, const void* base, int S, int B, long long ss, long long sb);
+
+constexpr int kH = 8;    // heads
+constexpr int kHD = 64;  // channels per head
+constexpr int kD = kH * kHD;
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// [B, S, 512] bf16 as a 3-D map (channel, token, sequence) whose box is one
+// head's [rows x 64] channels, 128-byte swizzle.
+bool encode_map(CUtensorMap* map, const void* base, int S, int B, long long ss, long long sb, int rows) {
+  cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)S, (cuuint64_t)B};
+  const long long sbb = B > 1 ? sb : (long long)S * ss;
+  cuuint64_t strides[2] = {(cuuint64_t)ss * 2, (cuuint64_t)sbb * 2};
+  cuuint32_t box[3] = {(cuuint32_t)kHD, (cuuint32_t)rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace fast
 }  // namespace ossm
+
+// The bf16 fast path applies: bf16 x, 8 heads of 64, Clenshaw evaluation with
+// the fused semantics, no tanh cache, 16-byte aligned rows (TMA).
+bool ossm_p3_eligible(const ossm_fwd_args* a) {
+  using namespace ossm::fast;
+  if (a->x_dtype != OSSM_BF16 || a->H != kH || a->head_dim != kHD || a->tanh_out) return false;
+  if ((a->flags & OSSM_EVAL_MASK) == OSSM_EVAL_LUT || (a->flags & (OSSM_F_FASTPATH | OSSM_F_GENERIC))) return false;
+  if (((uintptr_t)a->x % 16) || (a->x_stride_s % 8) || (a->B > 1 && (a->x_stride_b % 8))) return false;
+  if (a->out_dtype == OSSM_BF16 &&
+      (((uintptr_t)a->out % 16) || (a->out_stride_s % 8) || (a->B > 1 && (a->out_stride_b % 8))))
+    return false;
+  if (a->S > (1 << 30)) return false;
+  return encode_fn() != nullptr;
+}
 
 namespace ossm {
 namespace p3 {
@@ -49,8 +92,8 @@ namespace p3 {
 using namespace ev;
 
 constexpr int kNT = 256;
-constexpr int kH = 8;    // heads (one warp each)
-constexpr int kHD = 64;  // channels per head
+constexpr int kH = fast::kH;    // heads (one warp each)
+constexpr int kHD = fast::kHD;  // channels per head
 constexpr int kD = kH * kHD;
 constexpr int kBox = kL * 128;       // one head's [32 x 128 B] box
 constexpr int kTile = kH * kBox;     // 32 KB
@@ -97,6 +140,7 @@ struct Params {
   float* tot_A;           // [B*H] shard decay products (or NULL)
   float* tot_E;           // [B*H][64] shard end states from a zero state (or NULL)
   const float* carry_in;  // [B][D] state entering the shard (or NULL: zero / init_state)
+  float* shard_carry;     // [B][D] workspace slot where a sharded call folds carry_in
 };
 
 // w = hi + lo with hi = bf16(w) and lo = bf16(w - hi), for a pair of weights,
@@ -361,6 +405,26 @@ __global__ void __launch_bounds__(32) p3_blockfold_kernel(const Params p) {
   if (p.tot_A && lane == 0) p.tot_A[chain] = P;
 }
 
+// The state after the first `nshards` shards of a sequence-sharded call,
+// from the all-gathered shard totals [nshards][B*H decays | B*D end states]
+// and the state before the sequence (or zero): X_0 = init,
+// X_{q+1} = decay_q X_q + state_q, in shard order on every rank, so every
+// rank folds bitwise the same carries.  One thread per channel.
+__global__ void __launch_bounds__(256) shard_fold_kernel(int B, int H, int hd, int nshards, const float* totals,
+                                                         const float* init, float* state_out) {
+  const int D = H * hd;
+  const int i = (int)(blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= B * D) return;
+  const int b = i / D, h = (i - b * D) / hd;
+  const size_t stride = (size_t)B * H + (size_t)B * D;
+  float X = init ? __ldg(init + i) : 0.f;
+  for (int q = 0; q < nshards; ++q) {
+    const float* t = totals + (size_t)q * stride;
+    X = fmaf(__ldg(t + b * H + h), X, __ldg(t + (size_t)B * H + i));
+  }
+  state_out[i] = X;
+}
+
 // ---------------------------------------------------------------------------
 // pass 3: outputs from the carries
 // ---------------------------------------------------------------------------
@@ -503,6 +567,7 @@ size_t p3_single_bytes(const ossm_fwd_args* a) {
   size_t bytes = p3_al(sizeof(WsHeader)) + 2 * p3_al(N * 4) + 2 * p3_al(N * p3::kHD * 4) + 2 * p3_al(NB * 4) +
                  2 * p3_al(NB * p3::kHD * 4);
   bytes += p3_al((size_t)a->B * p3::kH * 4 * 32 * 16) + p3_al((size_t)p3::kH * 4 * 32 * 16);  // cmono, wfrag
+  bytes += p3_al((size_t)a->B * p3::kD * 4);  // the state entering a shard (sequence-sharded calls)
   if (a->gate_w && !a->lam_tok) bytes += p3_al((size_t)a->B * a->S * p3::kH * 4);
   return bytes;
 }
@@ -629,6 +694,8 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
   off += al((size_t)a->B * kH * 4 * 32 * 16);
   p.wfrag = reinterpret_cast<uint4*>(ws + off);
   off += al((size_t)kH * 4 * 32 * 16);
+  p.shard_carry = reinterpret_cast<float*>(ws + off);
+  off += al((size_t)a->B * kD * 4);
   p.lam_ws = gate ? reinterpret_cast<float*>(ws + off) : nullptr;
   p.starts_seq = 1;
   p.tot_A = nullptr;
@@ -642,7 +709,7 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
 int p3_aggregates(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
   using namespace p3;
   CUtensorMap mx;
-  if (!fast::encode_map(&mx, a->x, a->S, a->B, a->x_stride_s, a->x_stride_b)) return OSSM_EINVAL;
+  if (!fast::encode_map(&mx, a->x, a->S, a->B, a->x_stride_s, a->x_stride_b, kL)) return OSSM_EINVAL;
   const bool gate = a->gate_w && !a->lam_tok;
   const bool precise = (a->out_dtype == OSSM_F32) || (a->flags & OSSM_F_PRECISE);
   const int nprep = (precise ? 0 : a->B * kH) + (gate ? kH : 0);
@@ -820,11 +887,24 @@ int ossm_p3_shard_front(const ossm_fwd_args* a, int starts_sequence, char* ws, f
   return p3_front(a, p, st);
 }
 
-int ossm_p3_shard_back(const ossm_fwd_args* a, int starts_sequence, const float* carry_in, char* ws, cudaStream_t st) {
+int ossm_p3_shard_fold(int B, int H, int hd, int nshards, const float* totals, const float* init, float* state_out,
+                       cudaStream_t st) {
+  const int n = B * H * hd;
+  p3::shard_fold_kernel<<<(n + 255) / 256, 256, 0, st>>>(B, H, hd, nshards, totals, init, state_out);
+  return cudaGetLastError() == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
+}
+
+int ossm_p3_shard_back(const ossm_fwd_args* a, int shard, const float* totals, const float* seq_init, char* ws,
+                       cudaStream_t st) {
   p3::Params p;
   int r = p3_params(a, ws, p);
   if (r != OSSM_OK) return r;
-  p.starts_seq = starts_sequence ? 1 : 0;
-  p.carry_in = starts_sequence ? nullptr : carry_in;
+  p.starts_seq = shard == 0 ? 1 : 0;
+  p.carry_in = nullptr;
+  if (shard > 0) {  // the state entering this shard, folded on the device into the workspace
+    r = ossm_p3_shard_fold(a->B, p3::kH, p3::kHD, shard, totals, seq_init, p.shard_carry, st);
+    if (r != OSSM_OK) return r;
+    p.carry_in = p.shard_carry;
+  }
   return p3_back(a, p, st);
 }

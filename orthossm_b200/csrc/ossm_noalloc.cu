@@ -19,12 +19,18 @@
 //  * the first call on each GPU does the set-up (finds the array's device
 //    address and clears it on the caller's stream); make that first call
 //    before any other work that could overlap it, and before any stream
-//    capture.
+//    capture;
+//  * a call that takes the generic kernel (fp32 x or output, other head
+//    sizes, LUT) also clears that kernel's look-back flags in the array on
+//    the caller's stream first, because an earlier call of another shape may
+//    have left data there.
 #include <cuda_runtime.h>
 
 #include <mutex>
 
 #include "orthossm_b200.h"
+
+size_t ossm_fwd_flag_region(const ossm_fwd_args* a, size_t* offset);
 
 namespace {
 
@@ -40,7 +46,12 @@ void* g_scratch_ptr[kMaxDevices];  // device address of g_noalloc_scratch, per d
 
 extern "C" int ossm_cheby_ema_fwd_noalloc(const ossm_fwd_args* a, ossm_stream_t stream, void** scratch) {
   if (!a) return OSSM_EINVAL;
-  const size_t need = ossm_fwd_workspace_bytes(a);
+  // everything on the caller's stream: no side streams are created or used.
+  // The size check is made on these arguments, since the flag changes how
+  // the bf16 path lays out its scratch.
+  ossm_fwd_args one = *a;
+  one.flags |= OSSM_F_ONE_STREAM;
+  const size_t need = ossm_fwd_workspace_bytes(&one);
   if (need == 0) return OSSM_EINVAL;
   if (need > (size_t)OSSM_NOALLOC_SCRATCH_BYTES) return OSSM_EWORKSPACE;  // over the fixed maximum
 
@@ -53,10 +64,8 @@ extern "C" int ossm_cheby_ema_fwd_noalloc(const ossm_fwd_args* a, ossm_stream_t 
     std::lock_guard<std::mutex> lock(g_setup_mu);
     if (!g_scratch_ptr[dev]) {
       // set-up, once per device with that device current: the array's device
-      // address, then a clear (the look-back records and the launch counters
-      // must start at zero; afterwards every launch leaves its counters at
-      // zero and tags its records with a fresh epoch, so nothing is cleared
-      // again)
+      // address, then a clear (the launch header's counters must start at
+      // zero; every launch leaves them at zero again)
       void* p = nullptr;
       if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return OSSM_ELAUNCH;
       if (cudaMemsetAsync(p, 0, OSSM_NOALLOC_SCRATCH_BYTES, st) != cudaSuccess) return OSSM_ELAUNCH;
@@ -65,8 +74,9 @@ extern "C" int ossm_cheby_ema_fwd_noalloc(const ossm_fwd_args* a, ossm_stream_t 
     ptr = g_scratch_ptr[dev];
   }
   if (scratch) *scratch = ptr;
-  // everything on the caller's stream: no side streams are created or used
-  ossm_fwd_args one = *a;
-  one.flags |= OSSM_F_ONE_STREAM;
+  size_t flag_off = 0;
+  const size_t flag_bytes = ossm_fwd_flag_region(&one, &flag_off);
+  if (flag_bytes > 0 && cudaMemsetAsync(static_cast<char*>(ptr) + flag_off, 0, flag_bytes, st) != cudaSuccess)
+    return OSSM_ELAUNCH;
   return ossm_cheby_ema_fwd(&one, ptr, (size_t)OSSM_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -328,7 +328,7 @@ def _cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gat
     ``gate_decay``); overrides the gate.
     force_generic: run the generic kernel even where the TMA / tcgen05 path
     applies (bf16 x, head_dim 64); both compute the same function.
-    extra_flags: further OSSM_F_* kernel selections (e.g. OSSM_F_SINGLE_PASS),
+    extra_flags: further OSSM_F_* kernel selections (e.g. OSSM_F_ONE_STREAM),
     all computing the same function.
     Returns (out [B,S,D] in out_dtype (default x.dtype), final_state [B,D] f32)
     and the f32 tanh cache when ``return_tanh``."""
@@ -375,7 +375,10 @@ def fold_shard_carries(decays, states, upto, init=None):
 
 
 def exchange_shard_totals(decay, state, group=None):
-    """All-gather every rank's shard totals (one collective per tensor)."""
+    """All-gather every rank's shard totals; returns (decays, states), one
+    entry per rank.  The CUDA path packs both into one record and gathers
+    once (``cheby_ema_forward_seqpar``); this two-tensor form serves hosts
+    that fold on the CPU."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     decays = [torch.empty_like(decay) for _ in range(world)]
@@ -385,20 +388,50 @@ def exchange_shard_totals(decay, state, group=None):
     return decays, states
 
 
+def _shard_aggregate(a, starts, ws, record, B, H, stream):
+    """Step 1 of the sharded forward on this device: the shard's chunk
+    aggregates and carries, and its totals packed into ``record``
+    [B*H + B*D] (decays, then end states)."""
+    lib = L.lib()
+    L.check(lib.ossm_fwd_shard_aggregate(L.C.byref(a), int(starts), ws.data_ptr(), ws.numel(), record.data_ptr(),
+                                         record.data_ptr() + B * H * 4, stream.cuda_stream), "shard aggregate")
+
+
+def _shard_output(a, shard, ws, totals, seq_init, stream):
+    """Step 3: the state entering ``shard`` folded on the device from the
+    gathered ``totals`` [nshards, B*H + B*D] and ``seq_init``, then the
+    shard's outputs."""
+    lib = L.lib()
+    L.check(lib.ossm_fwd_shard_output(L.C.byref(a), int(shard), totals.data_ptr(), _ptr(seq_init), ws.data_ptr(),
+                                      ws.numel(), stream.cuda_stream), "shard output")
+
+
+def _shard_fold(B, H, hd, nshards, totals, seq_init, stream, out=None):
+    """The state after the first ``nshards`` shards, [B, H*hd] float32."""
+    lib = L.lib()
+    if out is None:
+        out = torch.empty(B, H * hd, device=totals.device, dtype=torch.float32)
+    L.check(lib.ossm_fwd_shard_fold(B, H, hd, int(nshards), totals.data_ptr(), _ptr(seq_init), out.data_ptr(),
+                                    stream.cuda_stream), "shard fold")
+    return out
+
+
 def cheby_ema_forward_seqpar(x, coeffs, *, group=None, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,
                              gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None,
                              eval_mode="clenshaw", precise=None, out=None):
     """``cheby_ema_forward`` over a sequence sharded across the ranks of
     ``group`` (torch.distributed, one GPU per rank): rank r holds tokens
     [r*S_shard, (r+1)*S_shard) of every sequence as ``x`` [B, S_shard, D]
-    (bf16, 8 heads of 64).  Each rank scans its shard, one all-gather
-    exchanges the shard totals ((H + D) floats per sequence per rank), each
-    rank folds the state entering its shard and writes its outputs.
+    (bf16, 8 heads of 64).  Each rank scans its shard from a zero state, one
+    all-gather exchanges the shard totals (B*(H + D) floats per rank, packed
+    in one record), and each rank folds the state entering its shard on the
+    device (in rank order, so every rank folds bitwise the same carries) and
+    writes its outputs.
 
-    ``init_state`` is the state before token 0 (used by rank 0; pass the same
-    tensor or None on every rank).  Returns (out [B, S_shard, D] bf16,
-    final_state [B, D] f32, the state after the last token of the whole
-    sequence, identical on every rank)."""
+    ``init_state`` is the state before token 0 (pass the same tensor or None
+    on every rank).  Returns (out [B, S_shard, D] bf16, final_state [B, D]
+    f32, the state after the last token of the whole sequence, identical on
+    every rank)."""
     import torch.distributed as dist
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     _need_cuda(x, coeffs)
@@ -417,17 +450,52 @@ def cheby_ema_forward_seqpar(x, coeffs, *, group=None, lambda_per_head=None, ema
         L.check(L.OSSM_EINVAL, "cheby_ema_forward_seqpar (argument check)")
     stream = torch.cuda.current_stream(dev)
     ws = _workspace(dev, stream, nbytes)
-    decay = torch.empty(B, H, device=dev, dtype=torch.float32)
-    state = torch.empty(B, D, device=dev, dtype=torch.float32)
-    L.check(lib.ossm_fwd_shard_aggregate(L.C.byref(a), int(rank == 0), ws.data_ptr(), ws.numel(), decay.data_ptr(),
-                                         state.data_ptr(), stream.cuda_stream), "shard aggregate")
-    decays, states = exchange_shard_totals(decay, state, group)
-    init = None if init_state is None else init_state.to(dev, torch.float32)
-    carry_in = fold_shard_carries(decays, states, rank, init).contiguous()
-    L.check(lib.ossm_fwd_shard_output(L.C.byref(a), int(rank == 0), carry_in.data_ptr(), ws.data_ptr(), ws.numel(),
-                                      stream.cuda_stream), "shard output")
-    final = fold_shard_carries(decays, states, world, init)
+    rec = B * H + B * D
+    record = torch.empty(rec, device=dev, dtype=torch.float32)
+    _shard_aggregate(a, rank == 0, ws, record, B, H, stream)
+    totals = torch.empty(world, rec, device=dev, dtype=torch.float32)
+    dist.all_gather_into_tensor(totals, record, group=group)
+    init = None if init_state is None else init_state.to(dev, torch.float32).contiguous()
+    _shard_output(a, rank, ws, totals, init, stream)
+    final = _shard_fold(B, H, D // H, world, totals, init, stream)
     del keep
+    return out, final
+
+
+def cheby_ema_forward_shards_local(x, coeffs, nshards, *, init_state=None, **kw):
+    """The sequence-sharded protocol of ``cheby_ema_forward_seqpar`` with all
+    ``nshards`` shards on this device (the all-gather becomes a copy): every
+    shard's aggregate pass, then every shard's output pass from the packed
+    totals.  Same arithmetic as a multi-GPU run, so it checks the sharded
+    path on one GPU.  x: [B, S, D] bf16; returns (out [B, S, D] bf16,
+    final_state [B, D])."""
+    _need_cuda(x, coeffs)
+    B, S, D = x.shape
+    H = coeffs.shape[1]
+    dev = x.device
+    stream = torch.cuda.current_stream(dev)
+    lib = L.lib()
+    bounds = [S * r // nshards for r in range(nshards + 1)]
+    init = None if init_state is None else init_state.to(dev, torch.float32).contiguous()
+    out = torch.empty(B, S, D, device=dev, dtype=torch.bfloat16)
+    rec = B * H + B * D
+    totals = torch.empty(nshards, rec, device=dev, dtype=torch.float32)
+    calls = []
+    for r in range(nshards):
+        xs = x[:, bounds[r]:bounds[r + 1]]
+        a, keep, o, f = _fwd_args(xs, coeffs, init_state=init if r == 0 else None, out_dtype=torch.bfloat16,
+                                  out=out[:, bounds[r]:bounds[r + 1]], **kw)
+        nb = lib.ossm_fwd_workspace_bytes(L.C.byref(a))
+        if nb == 0:
+            L.check(L.OSSM_EINVAL, "cheby_ema_forward_shards_local (argument check)")
+        ws = torch.zeros(nb, dtype=torch.uint8, device=dev)
+        _shard_aggregate(a, r == 0, ws, totals[r], B, H, stream)
+        calls.append((a, keep, ws))
+    for r, (a, keep, ws) in enumerate(calls):
+        _shard_output(a, r, ws, totals, init, stream)
+    final = _shard_fold(B, H, D // H, nshards, totals, init, stream)
+    torch.cuda.current_stream(dev).synchronize()
+    del calls
     return out, final
 
 

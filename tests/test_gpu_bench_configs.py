@@ -1,0 +1,132 @@
+"""Parity at the exact shapes bench.py times (BASELINE.json configs[1..3]).
+
+The CUDA path is compared, through the C ABI, with the oracle's C port
+(oracle/cheby_ref.c, fp32, the reference's sequential per-token scan, pinned
+to the float64 oracle and the reference goldens by test_oracle_cport.py) on
+the full workloads, and for the TTT with the float64 oracle on the first two
+full-size chunks.  Tolerances are those of BASELINE.json's north star:
+2e-2 relative (norm-wise) for bf16 I/O with fp32 state; the final fp32 state
+is held tighter, since only the carries' reassociation and tanh.approx's
+error reach it."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import cheby_ref as R
+from oracle import cref
+from tests.test_oracle_golden import relerr
+
+pytestmark = pytest.mark.gpu
+BF16_TOL = 2e-2
+LAMBDA = [0.9995, 0.9995, 0.997, 0.997, 0.995, 0.995, 0.95, 0.95]
+
+
+def _bits(t):
+    """bf16 tensor -> numpy uint16 bits (host)."""
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _chunked_relerr(a_bits, b_bits, rows=1 << 16):
+    """relerr of two bf16 bit arrays [B,S,D], accumulated over token blocks."""
+    num = den = 0.0
+    for s0 in range(0, a_bits.shape[1], rows):
+        a = cref.bf16_bits_to_f32(a_bits[:, s0:s0 + rows]).astype(np.float64)
+        b = cref.bf16_bits_to_f32(b_bits[:, s0:s0 + rows]).astype(np.float64)
+        num += float(((a - b) ** 2).sum())
+        den += float((b ** 2).sum())
+    return (num / max(den, 1e-300)) ** 0.5
+
+
+def test_config2_exact_bench_shape_vs_c_port():
+    """BASELINE configs[1] as bench.py runs it: B=8 x S=16384 x D=512, bf16 in
+    and out, fp32 state, the per-token gate, carried state N(0, 0.1), the
+    same seeded inputs; the default launch splits the batch over two
+    streams."""
+    import bench
+    import orthossm_b200 as O
+    x_bits = bench.x_bits_host(1234)
+    c, W, b, init = bench.small_inputs(1234)
+    lam = np.asarray(LAMBDA, np.float32)
+    x = torch.from_numpy(x_bits.view(np.int16)).view(torch.bfloat16).cuda()
+    out, fin = O.cheby_ema_forward(x, torch.from_numpy(c).cuda(), lambda_per_head=torch.tensor(LAMBDA).cuda(),
+                                   gate_weight=torch.from_numpy(W).cuda(), gate_bias=torch.from_numpy(b).cuda(),
+                                   init_state=torch.from_numpy(init).cuda())
+    torch.cuda.synchronize()
+    assert O.workspace_status() == 0
+    ref_bits, ref_fin = cref.forward(x_bits, c, lam=lam, gate=dict(W=W, b=b), init=init, out_bf16=True,
+                                     x_is_bf16_bits=True)
+    got = _bits(out)
+    assert _chunked_relerr(got, ref_bits) < BF16_TOL
+    assert relerr(fin.cpu().numpy(), ref_fin) < 1e-3
+    # per-element: no stray token (a wrong carry would show as a block of errors)
+    g = cref.bf16_bits_to_f32(got[:, ::97]).astype(np.float64)
+    r = cref.bf16_bits_to_f32(ref_bits[:, ::97]).astype(np.float64)
+    assert np.abs(g - r).max() < 0.05
+
+
+def test_config3_exact_million_tokens_vs_c_port():
+    """one sequence of 1,048,576 tokens, bf16, per-head
+    decays, no gate, from a zero state; the output and the final state
+    against the C port's sequential scan (the default launch runs the
+    sequence as two token ranges on two streams)."""
+    import orthossm_b200 as O
+    S = 1 << 20
+    g = torch.Generator(device="cuda").manual_seed(99)
+    x = torch.randn(1, S, 512, generator=g, device="cuda").to(torch.bfloat16)
+    c = (torch.randn(1, 8, 8, 64, generator=g, device="cuda") / torch.arange(1, 9, device="cuda").view(1, 1, 8, 1))
+    out, fin = O.cheby_ema_forward(x, c, lambda_per_head=torch.tensor(LAMBDA, device="cuda"))
+    torch.cuda.synchronize()
+    assert O.workspace_status() == 0
+    ref_bits, ref_fin = cref.forward(_bits(x), c.cpu().numpy(), lam=np.asarray(LAMBDA, np.float32),
+                                     out_bf16=True, x_is_bf16_bits=True)
+    assert _chunked_relerr(_bits(out), ref_bits) < BF16_TOL
+    assert relerr(fin.cpu().numpy(), ref_fin) < 1e-3
+
+
+def test_config3_eight_shards_on_one_gpu_vs_c_port():
+    """The sequence-sharded form of configs[2] (8 shards of 131,072 tokens),
+    emulated on one GPU through the shard entry points and the device fold,
+    against the same sequential scan."""
+    import orthossm_b200 as O
+    from orthossm_b200.sdpc_kernel import cheby_ema_forward_shards_local
+    S, G = 1 << 20, 8
+    g = torch.Generator(device="cuda").manual_seed(98)
+    x = torch.randn(1, S, 512, generator=g, device="cuda").to(torch.bfloat16)
+    c = (torch.randn(1, 8, 8, 64, generator=g, device="cuda") / torch.arange(1, 9, device="cuda").view(1, 1, 8, 1))
+    init = 0.1 * torch.randn(1, 512, generator=g, device="cuda")
+    lam = torch.tensor(LAMBDA, device="cuda")
+    out, fin = cheby_ema_forward_shards_local(x, c, G, lambda_per_head=lam, init_state=init)
+    torch.cuda.synchronize()
+    assert O.workspace_status() == 0
+    ref_bits, ref_fin = cref.forward(_bits(x), c.cpu().numpy(), lam=np.asarray(LAMBDA, np.float32),
+                                     init=init.cpu().numpy(), out_bf16=True, x_is_bf16_bits=True)
+    assert _chunked_relerr(_bits(out), ref_bits) < BF16_TOL
+    assert relerr(fin.cpu().numpy(), ref_fin) < 1e-3
+
+
+def test_config4_full_size_first_two_chunks_vs_oracle():
+    """BASELINE configs[3] at its full batch and chunk size (B=4, chunks of
+    2048 tokens, W_pred 512x512 std 0.02, Adam lr 1e-3): the first two chunk
+    steps of the 32768-token sequences against the float64 oracle."""
+    import orthossm_b200 as O
+    B, chunk, n = 4, 2048, 2
+    S = chunk * n
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(B, 32768, 512, generator=g)[:, :S].to(torch.bfloat16)
+    c = (torch.randn(B, 8, 8, 64, generator=g) / torch.arange(1, 9).view(1, 1, 8, 1))
+    Wp = torch.randn(512, 512, generator=g) * 0.02
+    z = torch.zeros_like(c)
+    lam = np.asarray(LAMBDA, np.float32)
+    ours = O.ttt_wpred_adam(x.cuda(), c.cuda(), z.cuda(), z.cuda(), 0, Wp.cuda(), lambda_per_head=LAMBDA,
+                            chunk=chunk)
+    torch.cuda.synchronize()
+    ref = R.ttt_wpred_adam(x.float().numpy().astype(np.float64), c.numpy().astype(np.float64), z.numpy(),
+                           z.numpy(), 0, Wp.numpy().astype(np.float64), lam.astype(np.float64), chunk=chunk)
+    assert ours["step"] == ref["step"] == n
+    cn = ours["coeffs"].cpu().numpy()
+    moved = np.abs(cn - ref["c"]) > 1e-5  # against |update| ~ lr = 1e-3 per step
+    assert moved.mean() < 0.01, moved.mean()
+    assert relerr(ours["out"].cpu().numpy(), ref["out"]) < 5e-3
+    assert relerr(ours["final"].cpu().numpy(), ref["final"]) < 5e-3
+    assert relerr(ours["m"].cpu().numpy(), ref["m"]) < 2e-2
+    assert relerr(ours["v"].cpu().numpy(), ref["v"]) < 2e-2

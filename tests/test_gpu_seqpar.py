@@ -39,46 +39,46 @@ def _problem(B, S, seed):
 @pytest.mark.parametrize("B,S,G,gate", [(2, 4096, 2, True), (1, 3000, 4, True), (2, 2048, 4, False),
                                         (1, 40000, 8, True), (1, 70001, 2, True)])
 def test_shards_on_one_gpu_match_unsharded(B, S, G, gate):
+    """The sharded protocol with every shard on one GPU (aggregates, packed
+    totals, device fold, outputs) against the unsharded forward and the
+    oracle; the device fold against the host fold of the same totals."""
     import orthossm_b200 as O
-    from orthossm_b200.sdpc_kernel import _fwd_args, fold_shard_carries
+    from orthossm_b200.sdpc_kernel import cheby_ema_forward_shards_local, fold_shard_carries, _shard_fold
     x, c, W, b, init, lam = _problem(B, S, 900 + S + G)
     xb = _t(x, torch.bfloat16)
     kw = dict(lambda_per_head=lam.tolist())
     if gate:
         kw.update(gate_weight=_t(W), gate_bias=_t(b))
     full, fin_full = O.cheby_ema_forward(xb, _t(c), init_state=_t(init), **kw)
-    lib = L.lib()
-    stream = torch.cuda.current_stream().cuda_stream
-    bounds = [S * r // G for r in range(G + 1)]
-    outs, decays, states, calls = [], [], [], []
-    for r in range(G):
-        xs = xb[:, bounds[r]:bounds[r + 1]].contiguous()
-        a, keep, out, fin = _fwd_args(xs, _t(c), init_state=_t(init) if r == 0 else None,
-                                      out_dtype=torch.bfloat16, **kw)
-        nb = lib.ossm_fwd_workspace_bytes(C.byref(a))
-        ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
-        dec = torch.empty(B, 8, device="cuda")
-        st = torch.empty(B, 512, device="cuda")
-        assert lib.ossm_fwd_shard_aggregate(C.byref(a), int(r == 0), ws.data_ptr(), nb, dec.data_ptr(),
-                                            st.data_ptr(), stream) == L.OSSM_OK
-        decays.append(dec)
-        states.append(st)
-        calls.append((a, keep, out, fin, ws, nb, xs))
-    for r, (a, keep, out, fin, ws, nb, xs) in enumerate(calls):
-        carry = fold_shard_carries(decays, states, r, _t(init)).contiguous()
-        assert lib.ossm_fwd_shard_output(C.byref(a), int(r == 0), carry.data_ptr(), ws.data_ptr(), nb,
-                                         stream) == L.OSSM_OK
-        outs.append(out)
+    joined, fin = cheby_ema_forward_shards_local(xb, _t(c), G, init_state=_t(init), **kw)
     torch.cuda.synchronize()
-    joined = torch.cat(outs, dim=1).float().cpu().numpy()
-    ref = full.float().cpu().numpy()
-    assert np.abs(joined - ref).max() <= 2 ** -7
-    fin_fold = fold_shard_carries(decays, states, G, _t(init)).cpu().numpy()
-    assert relerr(fin_fold, fin_full.cpu().numpy()) < 1e-5
-    assert relerr(calls[-1][3].cpu().numpy(), fin_full.cpu().numpy()) < 1e-5  # last shard's own final state
+    j = joined.float().cpu().numpy()
+    assert np.abs(j - full.float().cpu().numpy()).max() <= 2 ** -7
+    assert relerr(fin.cpu().numpy(), fin_full.cpu().numpy()) < 1e-5
     o = R.cheby_ema_forward(x, c, lam=lam.astype(np.float64), gate=dict(W=W, b=b) if gate else None, init=init)
-    assert relerr(joined, o["out"]) < 2e-2
+    assert relerr(j, o["out"]) < 2e-2
+    assert relerr(fin.cpu().numpy(), o["final"]) < 1e-3
     assert O.workspace_status() == 0
+
+
+def test_device_fold_is_the_host_fold():
+    """ossm_fwd_shard_fold against fold_shard_carries on random packed
+    totals: the same fold order, so the same carries to fp32 rounding of
+    one multiply-add per shard."""
+    from orthossm_b200.sdpc_kernel import fold_shard_carries, _shard_fold
+    g = torch.Generator().manual_seed(5)
+    B, H, hd, G = 3, 8, 64, 8
+    D = H * hd
+    dec = torch.rand(G, B, H, generator=g) * 0.5 + 0.5
+    st = torch.randn(G, B, D, generator=g)
+    init = 0.1 * torch.randn(B, D, generator=g)
+    totals = torch.cat([dec.reshape(G, -1), st.reshape(G, -1)], dim=1).cuda()
+    stream = torch.cuda.current_stream()
+    for upto in range(G + 1):
+        dev = _shard_fold(B, H, hd, upto, totals, init.cuda(), stream).cpu()
+        host = fold_shard_carries(list(dec), list(st), upto, init)
+        assert torch.allclose(dev, host, rtol=1e-6, atol=1e-6), upto
+    assert torch.equal(_shard_fold(B, H, hd, 0, totals, None, stream).cpu(), torch.zeros(B, D))
 
 
 def test_shard_entry_points_reject_other_paths():

@@ -4,8 +4,10 @@ handed their input and output buffers).  It takes its scratch from a fixed
 array inside the library instead of a caller workspace, so it must give the
 same outputs as ossm_cheby_ema_fwd with a workspace, call after call.
 
-This file is collected last on purpose: it must pass in a fresh process (the
-first call sets the array up) and after every other test."""
+The tests pass whether they run alone in a fresh process (where their first
+call sets the array up) or after the rest of the suite.  The file is named to
+be collected last, so that a run which stops at its first failure has run
+every other test before it."""
 import ctypes as C
 
 import numpy as np
@@ -51,7 +53,7 @@ def _args(d, out, fin):
 def test_noalloc_matches_workspace_entry_point(x_dtype, out_dtype):
     """Two calls in a row through the fixed scratch against one call with a
     caller workspace: bf16 (the fast path; the bar is one bf16 step and fp32
-    rounding of the final state, which also covers its single-pass variant)
+    rounding of the final state)
     and fp32 (generic kernel, bitwise reproducible)."""
     lib = L.lib()
     torch.cuda.set_device(0)
@@ -111,3 +113,50 @@ def test_noalloc_rejects_sizes_over_the_fixed_scratch():
     assert lib.ossm_cheby_ema_fwd_noalloc(C.byref(a), stream, None) == L.OSSM_EWORKSPACE
     torch.cuda.synchronize()
     assert bool((out == 7.0).all())
+
+
+def test_noalloc_sizes_its_scratch_with_its_own_flags():
+    """The entry point keeps all work on the caller's stream (OSSM_F_ONE_STREAM),
+    which changes how the bf16 path lays out its scratch for one long
+    sequence.  Its size limit must be checked on those flags: for B = 1 and a
+    long S the one-stream layout is never larger than the default one."""
+    lib = L.lib()
+    torch.cuda.set_device(0)
+    D = 512
+    for S in (4095 * 32, 4096 * 32, 4096 * 32 + 777, 1 << 18):
+        a = L.FwdArgs(B=1, S=S, H=8, head_dim=64, degree=8, x=1 << 20, x_dtype=L.OSSM_BF16,
+                      x_stride_b=S * D, x_stride_s=D, coeffs=1 << 20, momentum=0.9, out=1 << 20,
+                      out_dtype=L.OSSM_BF16, out_stride_b=S * D, out_stride_s=D)
+        default = lib.ossm_fwd_workspace_bytes(C.byref(a))
+        a.flags = L.OSSM_F_ONE_STREAM
+        one = lib.ossm_fwd_workspace_bytes(C.byref(a))
+        assert 0 < one <= default, S
+
+
+def test_noalloc_generic_kernel_across_shapes():
+    """fp32 calls (the generic kernel, whose look-back flags live in the
+    shared array) of two different shapes back to back, each against the
+    workspace entry point: the flags of one shape must not be read as
+    published records by the next."""
+    lib = L.lib()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream().cuda_stream
+    for B, S, seed in ((2, 3000, 1200), (3, 1111, 1300), (1, 5000, 1400), (2, 3000, 1200)):
+        d = _inputs(B, S, torch.float32, seed)
+        D = 512
+        out_ref = torch.empty(B, S, D, device="cuda")
+        fin_ref = torch.empty(B, D, device="cuda")
+        a = _args(d, out_ref, fin_ref)
+        nb = lib.ossm_fwd_workspace_bytes(C.byref(a))
+        ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+        assert lib.ossm_cheby_ema_fwd(C.byref(a), ws.data_ptr(), nb, stream) == L.OSSM_OK
+        out = torch.full((B, S, D), float("nan"), device="cuda")
+        fin = torch.full((B, D), float("nan"), device="cuda")
+        scratch = L._vp()
+        rc = lib.ossm_cheby_ema_fwd_noalloc(C.byref(_args(d, out, fin)), stream, C.byref(scratch))
+        assert rc == L.OSSM_OK, (B, S, lib.ossm_status_string(rc))
+        st = L._i32(-1)
+        assert lib.ossm_workspace_status(scratch, 1, stream, C.byref(st)) == L.OSSM_OK
+        assert st.value == L.OSSM_OK, (B, S)
+        assert relerr(out.cpu().numpy(), out_ref.cpu().numpy()) < 1e-6, (B, S)
+        assert relerr(fin.cpu().numpy(), fin_ref.cpu().numpy()) < 1e-6, (B, S)
