@@ -278,11 +278,19 @@ def run_ours(args):
         step(0)
         step(1)
     torch.cuda.synchronize()
-    # the bf16 head_dim-64 fast path: p3_prep_kernel, p3_agg_kernel, p3_carry_kernel,
-    # p3_out_kernel, once per group of sequences; a batch whose halves each hold
-    # >= 1024 (sequence, 32-token chunk) units runs as two halves on two streams
+    # the kernels this step runs: the grouped single-evaluation kernel (one
+    # launch), or the three-pass kernels (p3_prep, p3_agg, p3_carry, p3_out per
+    # group of sequences; a batch whose halves each hold >= 1024 (sequence,
+    # 32-token chunk) units runs as two halves on two streams)
+    path = O.forward_path(xs[0], c, lambda_per_head=lam, gate_weight=W, gate_bias=bvec, init_state=init)
     groups = 2 if B >= 2 and (B // 2) * ((S + 31) // 32) >= 1024 else 1
-    launches_per_step = 4 * groups
+    launches_per_step = 1 if path == "grouped" else 4 * groups
+    kernel_label = ("grp_fwd_kernel: one CTA per SM, each sequence owned by a group of CTAs, every element "
+                    "evaluated once, local states parked in TMEM, tile aggregates exchanged through a ring in "
+                    "global memory two rounds deep"
+                    if path == "grouped" else
+                    "forward step: p3_prep_kernel + p3_agg_kernel (gate + chunk aggregates) + p3_carry_kernel + "
+                    "p3_out_kernel" + (", two halves of the batch on two streams" if groups == 2 else ""))
 
     # ---- clocks: sample through a loaded soak and the timed region ----
     try:
@@ -368,6 +376,9 @@ def run_ours(args):
     e2e_value = world * B * S * e2e_steps / (e2e_ms / 1e3)
     status = O.workspace_status()
 
+    # ---- the opt-in single-evaluation kernel on the same step, for comparison ----
+    single = single_eval_record(args, xs, c, lam, W, bvec, init, outs, fin, stream, scan_bytes, max_over_ranks)
+
     # ---- BASELINE configs[2] sharded over the ranks (the sequence-parallel design) ----
     seqpar = seqpar_record(args, world, rank, dev, stream, barrier, max_over_ranks)
 
@@ -386,7 +397,7 @@ def run_ours(args):
             "config": config_dict(world),
             "gpu_launches": launches_per_step * K_eff,
             "hbm_gbs_step": (elem * 4 + B * D * 8) / (ms / K_eff / 1e3) / 1e9,
-            "roofline": {"bound": "hbm", "kernel": "forward step: p3_prep_kernel + p3_agg_kernel (gate + chunk aggregates) + p3_carry_kernel + p3_out_kernel" + (", two halves of the batch on two streams" if groups == 2 else ""), "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": kernel_label, "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                          "peak_kind": peak_kind, "bytes_per_step": scan_bytes,
                          "avg_step_ms": scan_avg},
@@ -398,10 +409,52 @@ def run_ours(args):
         if cpu is not None:
             line["cpu_baseline"] = cpu
         line["seqpar"] = seqpar
+        line["single_eval"] = single
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
         dist.destroy_process_group()
+
+
+def single_eval_record(args, xs, c, lam, W, bvec, init, outs, fin, stream, scan_bytes, max_over_ranks):
+    """The same config-2 step through the opt-in single-evaluation grouped
+    kernel (OSSM_F_SINGLE_EVAL: x read and every element evaluated once, one
+    CTA per SM, tile aggregates exchanged through the workspace): per-step
+    CUDA events (plain launches), max over ranks, and its largest output
+    difference from the default three-pass step on the same inputs."""
+    import torch
+    import orthossm_b200 as O
+    from orthossm_b200 import _lib as L
+    from orthossm_b200.sdpc_kernel import _cheby_ema_forward
+    kw = dict(lambda_per_head=lam, gate_weight=W, gate_bias=bvec, init_state=init)
+    if O.forward_path(xs[0], c, extra_flags=L.OSSM_F_SINGLE_EVAL, **kw) != "grouped":
+        return {"available": False}
+    steps = max(4, min(args.steps, 20))
+
+    def step(i):
+        _cheby_ema_forward(xs[i % 2], c, out=outs[i % 2], final_state=fin, extra_flags=L.OSSM_F_SINGLE_EVAL, **kw)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        torch.cuda._sleep(50_000_000)
+        for i, (a, bnd) in enumerate(evs):
+            a.record(stream)
+            step(i)
+            bnd.record(stream)
+    torch.cuda.synchronize()
+    us = max_over_ranks(sum(a.elapsed_time(bnd) for a, bnd in evs) / steps) * 1e3
+    with torch.cuda.stream(stream):
+        o1, f1 = _cheby_ema_forward(xs[0], c, extra_flags=L.OSSM_F_SINGLE_EVAL, **kw)
+        o3, f3 = _cheby_ema_forward(xs[0], c, **kw)
+    torch.cuda.synchronize()
+    peak, _ = peaks()
+    return {"available": True, "kernel": "grp_fwd_kernel (OSSM_F_SINGLE_EVAL)", "us_per_step": us,
+            "tokens_per_s": B * S / (us * 1e-6), "hbm_frac": scan_bytes / (us * 1e-6) / 1e9 / peak,
+            "max_abs_diff_vs_three_pass": (o1.float() - o3.float()).abs().max().item(),
+            "final_state_relerr_vs_three_pass": ((f1 - f3).norm() / f3.norm()).item(),
+            "device_status": O.workspace_status()}
 
 
 def seqpar_record(args, world, rank, dev, stream, barrier, max_over_ranks):

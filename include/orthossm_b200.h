@@ -62,6 +62,15 @@ enum ossm_dtype { OSSM_F32 = 0, OSSM_BF16 = 1 };
 /* Use the generic forward kernel even where the TMA / tcgen05 path applies
  * (the two paths compute the same function; used to test one against the other). */
 #define OSSM_F_GENERIC (1u << 4)
+/* On the bf16 fast path with bf16 output and 8 to (SM count) sequences, use
+ * the single-evaluation grouped kernel (x read and every element evaluated
+ * once: one cooperative launch, one CTA per SM, each sequence owned by a
+ * group of CTAs that exchange tile aggregates through the workspace) instead
+ * of the default three-pass kernels (chunk aggregates, carry scan, outputs;
+ * x read and evaluated twice).  Same function; the two differ only in the
+ * fp32 rounding of the carried state.  Measured on B200 at BASELINE.json
+ * configs[1] it is slower than the three-pass path, so it is opt-in. */
+#define OSSM_F_SINGLE_EVAL (1u << 5)
 /* Keep all of the call's work on the caller's stream: no side streams, so the
  * bf16 forward of a large batch does not split into two halves (same results,
  * bitwise) and one long sequence (at least 4096 chunks of 32 tokens) does not
@@ -108,6 +117,18 @@ typedef struct {
 size_t ossm_fwd_workspace_bytes(const ossm_fwd_args* a);
 int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_t workspace_bytes,
                        ossm_stream_t stream);
+
+/* Which kernels ossm_cheby_ema_fwd runs for these arguments on the current
+ * device (no launch): the generic kernel (any dtype / head size / mode), the
+ * three-pass bf16 kernels (chunk aggregates, carry scan, outputs: 4 launches
+ * per group of sequences), or the single-evaluation grouped kernel (one
+ * cooperative launch, one CTA per SM, each sequence owned by a group of CTAs
+ * that exchange tile aggregates through the workspace); -1 for invalid
+ * arguments. */
+#define OSSM_PATH_GENERIC 0
+#define OSSM_PATH_THREE_PASS 1
+#define OSSM_PATH_GROUPED 2
+int ossm_fwd_path(const ossm_fwd_args* a);
 
 /* ossm_cheby_ema_fwd for callers that cannot allocate device memory (a host
  * whose allocator owns all device memory, a plugin that is only handed its

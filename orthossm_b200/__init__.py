@@ -7,7 +7,8 @@ Public API mirrors the reference's ``sdpc_kernel`` op surface; see
 from .sdpc_kernel import (  # noqa: F401
     BASELINE_LAMBDA, LUT_TABLE_SIZE, MAX_DEGREE, MULTI_SCALE_LAMBDA, FusedChebyRKVv10,
     GatedComplexityPredictor, apply_cheby_rkv_core, apply_cheby_rkv_v10, cheby_ema_forward,
-    cheby_ema_forward_host, cheby_ema_forward_seqpar, cheby_ema_forward_shards_local, exchange_shard_totals, fold_shard_carries, gate_decay, get_chebyshev_lut,
+    cheby_ema_forward_host, cheby_ema_forward_seqpar, cheby_ema_forward_shards_local, exchange_shard_totals, fold_shard_carries, forward_path, gate_decay,
+    get_chebyshev_lut,
     init_chebyshev_coefficients, ttt_wpred_adam, workspace_status,
 )
 

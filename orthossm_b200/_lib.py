@@ -17,11 +17,13 @@ OSSM_EVAL_CLENSHAW, OSSM_EVAL_LUT, OSSM_EVAL_CLENSHAW_DEG4 = 0, 1, 2
 OSSM_F_FASTPATH = 1 << 2
 OSSM_F_PRECISE = 1 << 3
 OSSM_F_GENERIC = 1 << 4
+OSSM_F_SINGLE_EVAL = 1 << 5
 OSSM_F_ONE_STREAM = 1 << 7
 OSSM_NOALLOC_SCRATCH_BYTES = 16 << 20
+OSSM_PATH_GENERIC, OSSM_PATH_THREE_PASS, OSSM_PATH_GROUPED = 0, 1, 2
 
 EXPORTED = (
-    "ossm_fwd_workspace_bytes", "ossm_cheby_ema_fwd", "ossm_cheby_ema_fwd_noalloc", "ossm_gate_decay",
+    "ossm_fwd_workspace_bytes", "ossm_fwd_path", "ossm_cheby_ema_fwd", "ossm_cheby_ema_fwd_noalloc", "ossm_gate_decay",
     "ossm_fwd_host_workspace_bytes", "ossm_cheby_ema_fwd_host",
     "ossm_workspace_status", "ossm_fwd_shard_aggregate", "ossm_fwd_shard_output", "ossm_fwd_shard_fold",
     "ossm_cheby_rkv_lion", "ossm_version", "ossm_status_string",
@@ -89,6 +91,8 @@ _lib = None
 def _declare(lib):
     lib.ossm_fwd_workspace_bytes.restype = C.c_size_t
     lib.ossm_fwd_workspace_bytes.argtypes = [C.POINTER(FwdArgs)]
+    lib.ossm_fwd_path.restype = C.c_int
+    lib.ossm_fwd_path.argtypes = [C.POINTER(FwdArgs)]
     lib.ossm_cheby_ema_fwd.restype = C.c_int
     lib.ossm_cheby_ema_fwd.argtypes = [C.POINTER(FwdArgs), _vp, C.c_size_t, _vp]
     lib.ossm_cheby_ema_fwd_noalloc.restype = C.c_int

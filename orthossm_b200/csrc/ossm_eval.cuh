@@ -39,14 +39,16 @@ OSSM_DEV void cheb_to_mono(const float2 (&ck)[8], float gamma, float2 (&a)[8]) {
 }
 
 // The lane's two channels (j0, j0+1 of head h; 8 heads of 64) of the
-// coefficients [B,8,K,64]: raw (precise), or gamma-folded monomial scaled by
+// coefficients [B,8,Kd,64] (Kd = the tensor's degree), of which the first K
+// are used (K < Kd in the degree-4 truncation mode): raw (precise), or
+// gamma-folded monomial scaled by
 // 4^-k for Horner in z = 4 xn (power-of-two scaling: the same roundings as
 // Horner in xn on the unscaled monomial coefficients).
 // Held as (channel j0, channel j0+1) pairs, the operand layout of the packed
 // fp32x2 Horner.
 template <bool PRECISE>
-OSSM_DEV void load_coeffs(const float* coeffs, int K, int b, int h, int j0, float gamma, float2 (&m)[8]) {
-  const float* cb = coeffs + ((size_t)(b * 8 + h) * K) * 64 + j0;
+OSSM_DEV void load_coeffs(const float* coeffs, int Kd, int K, int b, int h, int j0, float gamma, float2 (&m)[8]) {
+  const float* cb = coeffs + ((size_t)(b * 8 + h) * Kd) * 64 + j0;
   float2 ck[8], cf[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q)

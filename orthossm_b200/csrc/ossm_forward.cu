@@ -420,6 +420,9 @@ using namespace ossm;
 
 bool ossm_p3_eligible(const ossm_fwd_args* a);
 size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a);
+bool ossm_grp_eligible(const ossm_fwd_args* a);
+size_t ossm_grp_workspace_bytes(const ossm_fwd_args* a);
+int ossm_grp_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
 int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
 int ossm_p3_shard_front(const ossm_fwd_args* a, int starts_sequence, char* ws, float* shard_decay, float* shard_state,
                         cudaStream_t st);
@@ -493,7 +496,8 @@ FwdLayout fwd_layout(const ossm_fwd_args* a) {
   l.off_lam = off;
   if (a->gate_w && !a->lam_tok) off = align256(off + (size_t)a->B * a->S * a->H * 4);
   l.total = off;
-  if (ossm_p3_eligible(a)) l.total = ossm_p3_workspace_bytes(a);  // the bf16 fast path
+  if (ossm_p3_eligible(a))  // the bf16 fast paths
+    l.total = ossm_grp_eligible(a) ? ossm_grp_workspace_bytes(a) : ossm_p3_workspace_bytes(a);
   return l;
 }
 
@@ -541,6 +545,12 @@ cudaError_t launch_gate(const ossm_fwd_args* a, float* lam_tok, cudaStream_t st)
 extern "C" size_t ossm_fwd_workspace_bytes(const ossm_fwd_args* a) {
   if (validate_fwd(a) != OSSM_OK) return 0;
   return fwd_layout(a).total;
+}
+
+extern "C" int ossm_fwd_path(const ossm_fwd_args* a) {
+  if (validate_fwd(a) != OSSM_OK) return -1;
+  if (!ossm_p3_eligible(a)) return OSSM_PATH_GENERIC;
+  return ossm_grp_eligible(a) ? OSSM_PATH_GROUPED : OSSM_PATH_THREE_PASS;
 }
 
 // Library-internal: where the generic kernel's look-back flags sit in the
@@ -600,7 +610,7 @@ extern "C" int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_
   p.incB = reinterpret_cast<float*>(ws + l.off_incB);
   p.nctas = (uint32_t)l.N;
 
-  if (ossm_p3_eligible(a)) return ossm_p3_launch(a, ws, st);
+  if (ossm_p3_eligible(a)) return ossm_grp_eligible(a) ? ossm_grp_launch(a, ws, st) : ossm_p3_launch(a, ws, st);
 
   if (a->gate_w && !a->lam_tok) {
     if (launch_gate(a, reinterpret_cast<float*>(ws + l.off_lam), st) != cudaSuccess) return OSSM_ELAUNCH;

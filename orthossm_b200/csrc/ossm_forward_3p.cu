@@ -109,7 +109,7 @@ constexpr int kPer = 16;                             // carry kernel: chunks per
 constexpr int kBlk = kSpans * kPer;                  // chunks per carry block
 
 struct Params {
-  int B, S, K, nchunks;
+  int B, S, K, Kd, nchunks;  // K degrees used of the coefficient tensor's Kd
   const __nv_bfloat16* x;
   long long xsb, xss;
   const float* coeffs;
@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(32) p3_prep_kernel(const Params p) {
     const int b = blockIdx.x / kH, h = blockIdx.x % kH;
     const float gamma = 0.98f - 0.06f * (float)h / (float)kH;
     float2 cm[8];
-    load_coeffs<false>(p.coeffs, p.K, b, h, lane * 2, gamma, cm);
+    load_coeffs<false>(p.coeffs, p.Kd, p.K, b, h, lane * 2, gamma, cm);
     float4* dst = p.cmono + (size_t)blockIdx.x * 4 * 32 + lane;
 #pragma unroll
     for (int q = 0; q < 4; ++q) dst[q * 32] = make_float4(cm[2 * q].x, cm[2 * q].y, cm[2 * q + 1].x, cm[2 * q + 1].y);
@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
   // p3_prep_kernel on the fast path), the caller's decay
   float2 cm[8];
   if (PRECISE)
-    load_coeffs<true>(p.coeffs, p.K, b, h, j0, gamma, cm);
+    load_coeffs<true>(p.coeffs, p.Kd, p.K, b, h, j0, gamma, cm);
   else
     load_mono(p, b, h, lane, cm);
   const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(kNT, PRECISE ? 3 : 4) p3_out_kernel(const Para
   lam_s[h * kL + lane] = make_float2(lam, 1.f - lam);
   float2 cm[8];
   if (PRECISE)
-    load_coeffs<true>(p.coeffs, p.K, b, h, j0, gamma, cm);
+    load_coeffs<true>(p.coeffs, p.Kd, p.K, b, h, j0, gamma, cm);
   else
     load_mono(p, b, h, lane, cm);
   __syncwarp();
@@ -649,6 +649,7 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
   p.B = a->B;
   p.S = a->S;
   p.K = (a->flags & OSSM_EVAL_MASK) == OSSM_EVAL_CLENSHAW_DEG4 ? (a->degree < 4 ? a->degree : 4) : a->degree;
+  p.Kd = a->degree;
   p.nchunks = (a->S + kL - 1) / kL;
   p.x = reinterpret_cast<const __nv_bfloat16*>(a->x);
   p.xsb = a->x_stride_b;

@@ -57,6 +57,11 @@ ossm_fwd_args part_args(const ossm_fwd_args& a, const Part& p, void* x, void* ou
   const long long D = (long long)a.H * a.head_dim;
   const int mb = p.b1 - p.b0, ms = p.s1 - p.s0;
   ossm_fwd_args r = a;
+  // Every part runs on the three-pass kernels, whatever its number of
+  // sequences, so the result does not depend on how the batch was cut (and
+  // whole-sequence parts give bitwise the forward of the batch).  The call
+  // is bound by the host link, not by the kernel.
+  r.flags &= ~OSSM_F_SINGLE_EVAL;
   r.B = mb;
   r.S = ms;
   r.x = x;

@@ -224,6 +224,17 @@ def _fwd_args(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=
     return a, keep, out, final_state
 
 
+def forward_path(x, coeffs, **kw):
+    """Which kernels ``cheby_ema_forward(x, coeffs, **kw)`` runs on x's device:
+    "generic", "three_pass" or "grouped" (no launch)."""
+    a, keep, _, _ = _fwd_args(x, coeffs, **kw)
+    r = L.lib().ossm_fwd_path(L.C.byref(a))
+    del keep
+    if r < 0:
+        L.check(L.OSSM_EINVAL, "forward_path (argument check)")
+    return {L.OSSM_PATH_GENERIC: "generic", L.OSSM_PATH_THREE_PASS: "three_pass", L.OSSM_PATH_GROUPED: "grouped"}[r]
+
+
 def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,
                       gate_bias=None, gate_scale=0.008, gate_range=(0.0, 1.0), init_state=None,
                       out_dtype=None, return_tanh=False, eval_mode="clenshaw",

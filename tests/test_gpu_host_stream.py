@@ -10,6 +10,13 @@ from tests.golden.inputs import det_normal, linear_init, spectral_coeffs
 pytestmark = pytest.mark.gpu
 
 
+def _device_ref(x, c, **kw):
+    """The one-call device forward (the three-pass kernels, which the
+    host-buffer call runs its parts on)."""
+    import orthossm_b200 as O
+    return O.cheby_ema_forward(x, c, **kw)
+
+
 def _inputs(B, S, seed):
     D, H = 512, 8
     x = torch.from_numpy(R.bf16_round(det_normal((B, S, D), seed)).astype(np.float32)).to(torch.bfloat16)
@@ -26,7 +33,7 @@ def test_host_stream_matches_device_call(B, S, pieces):
     x, c, W, b, init = _inputs(B, S, 3000 + B * S)
     lam = list(R.BASELINE_LAMBDA)
     kw = dict(lambda_per_head=lam, gate_weight=W.cuda(), gate_bias=b.cuda())
-    ref, fin = O.cheby_ema_forward(x.cuda(), c.cuda(), init_state=init.cuda(), **kw)
+    ref, fin = _device_ref(x.cuda(), c.cuda(), init_state=init.cuda(), **kw)
     out_h, fin_h = O.cheby_ema_forward_host(x.pin_memory(), c.cuda(), init_state=init.cuda(), pieces=pieces, **kw)
     torch.cuda.synchronize()
     assert out_h.is_pinned() and out_h.dtype == torch.bfloat16
@@ -49,7 +56,7 @@ def test_host_stream_per_token_decay_is_cut_with_the_parts(B, pieces):
     g = torch.Generator().manual_seed(5)
     lt = (0.9 + 0.1 * torch.rand(B, S, 8, generator=g)).cuda()
     kw = dict(lambda_per_head=list(R.BASELINE_LAMBDA), lam_tok=lt)
-    ref, fin = O.cheby_ema_forward(x.cuda(), c.cuda(), init_state=init.cuda(), **kw)
+    ref, fin = _device_ref(x.cuda(), c.cuda(), init_state=init.cuda(), **kw)
     out_h, fin_h = O.cheby_ema_forward_host(x.pin_memory(), c.cuda(), init_state=init.cuda(), pieces=pieces, **kw)
     torch.cuda.synchronize()
     _check(out_h, fin_h, ref, fin, whole=B >= pieces)
@@ -66,7 +73,7 @@ def test_c_abi_host_call_with_pageable_buffers():
     B, S = 3, 1500
     x, c, W, b, init = _inputs(B, S, 11)
     kw = dict(lambda_per_head=list(R.BASELINE_LAMBDA), gate_weight=W.cuda(), gate_bias=b.cuda())
-    ref, fin = O.cheby_ema_forward(x.cuda(), c.cuda(), init_state=init.cuda(), **kw)
+    ref, fin = _device_ref(x.cuda(), c.cuda(), init_state=init.cuda(), **kw)
     out_h, fin_h = torch.empty_like(x), torch.empty(B, 512)
     a, keep, _, _ = _fwd_args(x.contiguous(), c.cuda(), init_state=init.contiguous(), out=out_h, final_state=fin_h,
                               host=True, device="cuda", **kw)
