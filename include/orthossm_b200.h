@@ -325,6 +325,49 @@ typedef struct {
 size_t ossm_ttt_workspace_bytes(const ossm_ttt_args* a);
 int ossm_ttt_wpred_step(const ossm_ttt_args* a, void* workspace, size_t workspace_bytes, ossm_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * BASELINE-mode TTT over a whole sequence in one call (BASELINE.json
+ * configs[3]; no counterpart in the reference).  For each chunk of `chunk`
+ * tokens, in order: the gate's per-token decays (gate_w != NULL), the forward
+ * with fp32 states into out[:, chunk] (carried state across chunks, starting
+ * from init_state), gs_t = (2/N) W_pred^T (W_pred s_t - x_{t+1}) for t < L-1
+ * (N = (L-1) D), and ossm_ttt_wpred_step's reverse adjoint, gradient and Adam
+ * with step number step0 + chunk index + 1.  gs is formed on the tensor cores
+ * by one kernel per chunk as (2/N) (G s_t - W_pred^T x_{t+1}) with
+ * G = W_pred^T W_pred (exact fp32, formed once per call): s . G as a TF32
+ * product, x . W_pred as bf16 x times W_pred split into two bf16 terms (fp32
+ * x: one TF32 product).  H * head_dim must be a multiple of 256; x needs
+ * 16-byte aligned rows.  out is [B,S,H*head_dim] fp32, contiguous.
+ * The workspace (ossm_ttt_run_workspace_bytes) must be zero-filled once when
+ * first allocated; its first 256 bytes are a header that
+ * ossm_workspace_status reads.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  int32_t B, S, H, head_dim, degree, chunk;
+  const void* x;                     /* [B,S,H*head_dim] */
+  int32_t x_dtype;
+  int64_t x_stride_b, x_stride_s;
+  float* coeffs;                     /* [B,H,degree,head_dim], in/out */
+  float* m;                          /* Adam first moment, in/out */
+  float* v;                          /* Adam second moment, in/out */
+  const float* lam_h;                /* [H] or NULL (momentum) */
+  float momentum;
+  const float* gate_w;               /* [H, H*head_dim] or NULL (no gate) */
+  const float* gate_b;               /* [H] (with gate_w) */
+  float gate_scale, gate_lo, gate_hi;
+  const float* w_pred;               /* [D,D] fp32, row-major */
+  const float* init_state;           /* [B,D] or NULL (zeros) */
+  float* final_state;                /* [B,D] or NULL: the state after the last token */
+  float* out;                        /* [B,S,D] fp32 contiguous: the states */
+  float lr, beta1, beta2, eps, spectral_pow;
+  int32_t step0;                     /* Adam steps already taken */
+  int32_t forget;                    /* 1: forget gate lam_h on c */
+  uint32_t flags;                    /* forward flags (OSSM_EVAL_*) */
+} ossm_ttt_run_args;
+
+size_t ossm_ttt_run_workspace_bytes(const ossm_ttt_run_args* a);
+int ossm_ttt_wpred_run(const ossm_ttt_run_args* a, void* workspace, size_t workspace_bytes, ossm_stream_t stream);
+
 /* Library metadata. */
 const char* ossm_version(void);
 const char* ossm_status_string(int status);
@@ -333,6 +376,7 @@ size_t ossm_sizeof_fwd_args(void);
 size_t ossm_sizeof_lion_args(void);
 size_t ossm_sizeof_ttt_args(void);
 size_t ossm_sizeof_bwd_args(void);
+size_t ossm_sizeof_ttt_run_args(void);
 
 #ifdef __cplusplus
 }

@@ -29,7 +29,7 @@ EXPORTED = (
     "ossm_cheby_rkv_lion", "ossm_version", "ossm_status_string",
     "ossm_sizeof_fwd_args", "ossm_sizeof_lion_args", "ossm_sizeof_ttt_args",
     "ossm_ttt_workspace_bytes", "ossm_ttt_wpred_step", "ossm_sizeof_bwd_args", "ossm_bwd_workspace_bytes",
-    "ossm_cheby_ema_bwd",
+    "ossm_cheby_ema_bwd", "ossm_ttt_run_workspace_bytes", "ossm_ttt_wpred_run", "ossm_sizeof_ttt_run_args",
 )
 
 _vp = C.c_void_p
@@ -69,6 +69,18 @@ class TttArgs(C.Structure):
         ("coeffs", _vp), ("m", _vp), ("v", _vp), ("lam_h", _vp), ("momentum", _f32), ("lam_tok", _vp),
         ("gs", _vp), ("lr", _f32), ("beta1", _f32), ("beta2", _f32), ("eps", _f32), ("spectral_pow", _f32),
         ("step", _i32), ("forget", _i32),
+    ]
+
+
+class TttRunArgs(C.Structure):
+    _fields_ = [
+        ("B", _i32), ("S", _i32), ("H", _i32), ("head_dim", _i32), ("degree", _i32), ("chunk", _i32),
+        ("x", _vp), ("x_dtype", _i32), ("x_stride_b", _i64), ("x_stride_s", _i64),
+        ("coeffs", _vp), ("m", _vp), ("v", _vp), ("lam_h", _vp), ("momentum", _f32),
+        ("gate_w", _vp), ("gate_b", _vp), ("gate_scale", _f32), ("gate_lo", _f32), ("gate_hi", _f32),
+        ("w_pred", _vp), ("init_state", _vp), ("final_state", _vp), ("out", _vp),
+        ("lr", _f32), ("beta1", _f32), ("beta2", _f32), ("eps", _f32), ("spectral_pow", _f32),
+        ("step0", _i32), ("forget", _i32), ("flags", C.c_uint32),
     ]
 
 
@@ -128,6 +140,13 @@ def _declare(lib):
     lib.ossm_ttt_workspace_bytes.argtypes = [C.POINTER(TttArgs)]
     lib.ossm_ttt_wpred_step.restype = C.c_int
     lib.ossm_ttt_wpred_step.argtypes = [C.POINTER(TttArgs), _vp, C.c_size_t, _vp]
+    lib.ossm_ttt_run_workspace_bytes.restype = C.c_size_t
+    lib.ossm_ttt_run_workspace_bytes.argtypes = [C.POINTER(TttRunArgs)]
+    lib.ossm_ttt_wpred_run.restype = C.c_int
+    lib.ossm_ttt_wpred_run.argtypes = [C.POINTER(TttRunArgs), _vp, C.c_size_t, _vp]
+    lib.ossm_sizeof_ttt_run_args.restype = C.c_size_t
+    if lib.ossm_sizeof_ttt_run_args() != C.sizeof(TttRunArgs):
+        raise RuntimeError("orthossm_b200: ctypes struct layout does not match the C ABI")
     if (lib.ossm_sizeof_fwd_args() != C.sizeof(FwdArgs) or lib.ossm_sizeof_lion_args() != C.sizeof(LionArgs)
             or lib.ossm_sizeof_ttt_args() != C.sizeof(TttArgs) or lib.ossm_sizeof_bwd_args() != C.sizeof(BwdArgs)):
         raise RuntimeError("orthossm_b200: ctypes struct layout does not match the C ABI")

@@ -18,7 +18,7 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIBDIR = os.path.join(PKG, "_lib")
 LIBNAME = "liborthossm_b200.so"
-SOURCES = ["ossm_capi.cu", "ossm_forward.cu", "ossm_forward_3p.cu", "ossm_forward_grp.cu", "ossm_host.cu", "ossm_lion.cu", "ossm_noalloc.cu", "ossm_reverse.cu"]
+SOURCES = ["ossm_capi.cu", "ossm_forward.cu", "ossm_forward_3p.cu", "ossm_forward_grp.cu", "ossm_host.cu", "ossm_lion.cu", "ossm_noalloc.cu", "ossm_reverse.cu", "ossm_ttt.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

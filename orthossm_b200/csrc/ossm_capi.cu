@@ -19,3 +19,4 @@ extern "C" size_t ossm_sizeof_fwd_args(void) { return sizeof(ossm_fwd_args); }
 extern "C" size_t ossm_sizeof_lion_args(void) { return sizeof(ossm_lion_args); }
 extern "C" size_t ossm_sizeof_ttt_args(void) { return sizeof(ossm_ttt_args); }
 extern "C" size_t ossm_sizeof_bwd_args(void) { return sizeof(ossm_bwd_args); }
+extern "C" size_t ossm_sizeof_ttt_run_args(void) { return sizeof(ossm_ttt_run_args); }

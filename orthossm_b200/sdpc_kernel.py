@@ -602,10 +602,15 @@ def ttt_wpred_adam(x, coeffs, m, v, step, W_pred, *, lambda_per_head=None, ema_m
     mean_{t<L-1,d} (W_pred s_t - x_{t+1})^2 per sequence, its gradient through
     the EMA, tanh and Chebyshev basis, scaled by 1/(k+1)^spectral_pow, and one
     Adam step with the forget gate c <- lambda_h c - lr mhat/(sqrt(vhat)+eps).
-    The W_pred products run on cuBLAS: ``gemm="tf32"`` (default) on the tensor
-    cores with fp32 inputs and accumulation rounded through TF32, as the
-    spec's "BF16/TF32 GEMM" allows; ``gemm="fp32"`` keeps full fp32 (SIMT).
-    The adjoint, gradient and Adam run in ``ossm_ttt_wpred_step``.
+    ``gemm="tf32"`` (default): the whole chunk loop is one native call
+    (``ossm_ttt_wpred_run``): per chunk the gate, the forward, one tcgen05
+    kernel forming dL/ds = (2/N)(G s_t - W_pred^T x_{t+1}), G = W_pred^T W_pred
+    (s . G on TF32 tensor cores, x . W_pred with W_pred split into two bf16
+    terms), and the reverse adjoint / gradient / Adam of
+    ``ossm_ttt_wpred_step``; it needs H*head_dim a multiple of 256 and
+    16-byte aligned rows of x.  ``gemm="fp32"`` (or other shapes) runs the
+    chunk loop from Python with the two W_pred products on cuBLAS in full
+    fp32 (``"tf32"`` there: TF32 cuBLAS).
 
     x: [B,S,D] (CUDA, bf16 or fp32); coeffs, m, v: [B,H,K,hd] (not modified);
     step: Adam steps already taken.  Returns dict(out [B,S,D] fp32, coeffs, m,
@@ -627,6 +632,26 @@ def ttt_wpred_adam(x, coeffs, m, v, step, W_pred, *, lambda_per_head=None, ema_m
     stream = torch.cuda.current_stream(dev)
     xdt = x.dtype if x.dtype in _DT else torch.float32
     x = x.to(xdt)
+    if gemm == "tf32":
+        gw = gb = None
+        if gate_weight is not None:
+            gw = gate_weight.to(dev, torch.float32).contiguous()
+            gb = gate_bias.to(dev, torch.float32).contiguous()
+        fin = torch.empty(B, D, device=dev, dtype=torch.float32)
+        a = L.TttRunArgs(B=B, S=S, H=H, head_dim=hd, degree=K, chunk=int(chunk), x=x.data_ptr(), x_dtype=_DT[xdt],
+                         x_stride_b=x.stride(0), x_stride_s=x.stride(1), coeffs=c.data_ptr(), m=m.data_ptr(),
+                         v=v.data_ptr(), lam_h=lam.data_ptr(), momentum=float(ema_momentum), gate_w=_ptr(gw),
+                         gate_b=_ptr(gb), gate_scale=float(gate_scale), gate_lo=float(gate_range[0]),
+                         gate_hi=float(gate_range[1]), w_pred=Wp.data_ptr(), init_state=_ptr(state),
+                         final_state=fin.data_ptr(), out=out.data_ptr(), lr=float(lr), beta1=float(betas[0]),
+                         beta2=float(betas[1]), eps=float(eps), spectral_pow=float(spectral_pow), step0=int(step),
+                         forget=int(bool(forget)), flags=0)
+        nbytes = lib.ossm_ttt_run_workspace_bytes(L.C.byref(a))
+        if nbytes:
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+            L.check(lib.ossm_ttt_wpred_run(L.C.byref(a), ws.data_ptr(), nbytes, stream.cuda_stream), "ttt_wpred_run")
+            nch = (S + chunk - 1) // chunk
+            return dict(out=out, coeffs=c, m=m, v=v, step=step + nch, final=fin)
     for t0 in range(0, S, chunk):
         Lc = min(chunk, S - t0)
         xc = x[:, t0:t0 + Lc]

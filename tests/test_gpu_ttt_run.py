@@ -1,0 +1,107 @@
+"""The native BASELINE-mode TTT run (``ossm_ttt_wpred_run``: gate, forward,
+the tcgen05 W_pred gradient kernel, reverse adjoint and Adam per chunk, in one
+call) against the same chunk loop driven from Python with both W_pred
+products on cuBLAS in full fp32, and against the float64 oracle.
+
+The tensor-core kernel forms dL/ds = (2/N)(G s - W_pred^T x_{t+1}) with s . G
+as a TF32 product and x . W_pred split into two bf16 terms, so a single
+chunk's gradient (the Adam first moment after one step from zero) must agree
+with the fp32 loop to TF32 accuracy; over several chunks Adam's near-sign
+early steps let a few coefficients with a gradient at rounding level move the
+other way, which the bar allows for a small fraction."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import cheby_ref as R
+from tests.golden.inputs import det_normal, linear_init, spectral_coeffs
+from tests.test_oracle_golden import relerr
+
+pytestmark = pytest.mark.gpu
+
+
+def T(a, dt=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(a)).to("cuda", dt)
+
+
+def _inputs(B, S, H, hd, seed, gated, init):
+    D = H * hd
+    x = R.bf16_round(det_normal((B, S, D), seed)).astype(np.float32)
+    c = spectral_coeffs(B, H, 8, hd, seed + 1).astype(np.float32)
+    Wp = det_normal((D, D), seed + 2, 0.02).astype(np.float32)
+    W, b = linear_init(H, D, seed + 3)
+    ini = det_normal((B, D), seed + 4, 0.1).astype(np.float32) if init else None
+    lam = np.asarray(R.BASELINE_LAMBDA[:H] if H <= 8 else [0.9] * H, np.float32)
+    return x, c, Wp, W, b, ini, lam
+
+
+def _run(x, c, Wp, W, b, ini, lam, chunk, gemm, x_dt=torch.bfloat16):
+    import orthossm_b200 as O
+    z = np.zeros_like(c)
+    kw = dict(lambda_per_head=lam.tolist(), chunk=chunk, gemm=gemm)
+    if W is not None:
+        kw.update(gate_weight=T(W), gate_bias=T(b))
+    if ini is not None:
+        kw.update(init_state=T(ini))
+    r = O.ttt_wpred_adam(T(x, x_dt), T(c), T(z), T(z), 0, T(Wp), **kw)
+    torch.cuda.synchronize()
+    return {k: (v.cpu().numpy() if torch.is_tensor(v) else v) for k, v in r.items()}
+
+
+@pytest.mark.parametrize("B,S,H,chunk,gated,init,x_dt", [
+    (2, 128, 8, 128, False, False, torch.bfloat16),
+    (3, 300, 8, 300, True, True, torch.bfloat16),     # 3 token tiles, the last one ragged
+    (1, 257, 4, 257, False, True, torch.float32),     # D = 256, fp32 x (TF32 x-side product)
+])
+def test_first_chunk_gradient_matches_fp32_loop(B, S, H, chunk, gated, init, x_dt):
+    x, c, Wp, W, b, ini, lam = _inputs(B, S, H, 64, 2100 + S, gated, init)
+    if not gated:
+        W = b = None
+    nat = _run(x, c, Wp, W, b, ini, lam, chunk, "tf32", x_dt)
+    ref = _run(x, c, Wp, W, b, ini, lam, chunk, "fp32", x_dt)
+    assert nat["step"] == ref["step"] == 1
+    np.testing.assert_array_equal(nat["out"], ref["out"])  # the same forward kernels
+    np.testing.assert_array_equal(nat["final"], ref["final"])
+    assert relerr(nat["m"], ref["m"]) < 1e-3  # m = (1 - beta1) g after one step
+    assert relerr(nat["v"], ref["v"]) < 2e-3
+
+
+@pytest.mark.parametrize("gated", [False, True])
+def test_multi_chunk_run_matches_oracle(gated):
+    B, S, H, hd, chunk = 2, 700, 8, 64, 200  # four chunks, the last one 100 tokens
+    x, c, Wp, W, b, ini, lam = _inputs(B, S, H, hd, 2200, gated, True)
+    if not gated:
+        W = b = None
+    nat = _run(x, c, Wp, W, b, ini, lam, chunk, "tf32")
+    z = np.zeros_like(c)
+    ref = R.ttt_wpred_adam(x.astype(np.float64), c.astype(np.float64), z, z, 0, Wp.astype(np.float64),
+                           lam.astype(np.float64), gate=dict(W=W, b=b) if gated else None,
+                           init=ini.astype(np.float64), chunk=chunk)
+    assert nat["step"] == ref["step"] == 4
+    moved = np.abs(nat["coeffs"] - ref["c"]) > 1e-5
+    assert moved.mean() < 0.01, moved.mean()
+    assert relerr(nat["out"], ref["out"]) < 5e-3
+    assert relerr(nat["final"], ref["final"]) < 5e-3
+    assert relerr(nat["m"], ref["m"]) < 2e-2
+    assert relerr(nat["v"], ref["v"]) < 2e-2
+
+
+def test_run_single_token_chunks_and_inputs_untouched():
+    """chunk = 1 (no loss term: gs is never formed) and a last chunk of one
+    token; the caller's tensors are not modified."""
+    import orthossm_b200 as O
+    B, S, H, hd = 1, 5, 4, 64
+    x, c, Wp, W, b, ini, lam = _inputs(B, S, H, hd, 2300, False, False)
+    cT, mT, vT = T(c), T(np.zeros_like(c)), T(np.zeros_like(c))
+    for chunk in (1, 4):
+        r = O.ttt_wpred_adam(T(x, torch.bfloat16), cT, mT, vT, 0, T(Wp), lambda_per_head=lam.tolist(), chunk=chunk)
+        f = O.ttt_wpred_adam(T(x, torch.bfloat16), cT, mT, vT, 0, T(Wp), lambda_per_head=lam.tolist(), chunk=chunk,
+                             gemm="fp32")
+        torch.cuda.synchronize()
+        assert r["step"] == f["step"] == -(-S // chunk)
+        if chunk == 1:  # no gradient at all: Adam with g = 0 leaves m, v at zero; only the forget gate acts
+            np.testing.assert_array_equal(r["out"].cpu().numpy(), f["out"].cpu().numpy())
+            np.testing.assert_array_equal(r["coeffs"].cpu().numpy(), f["coeffs"].cpu().numpy())
+        else:
+            assert relerr(r["out"].cpu().numpy(), f["out"].cpu().numpy()) < 1e-3
+    assert np.array_equal(cT.cpu().numpy(), c) and not mT.abs().sum().item()
