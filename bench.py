@@ -382,6 +382,11 @@ def run_ours(args):
     # ---- BASELINE configs[2] sharded over the ranks (the sequence-parallel design) ----
     seqpar = seqpar_record(args, world, rank, dev, stream, barrier, max_over_ranks)
 
+    # ---- BASELINE configs[3], the reference's live Lion op, configs[4] ----
+    ttt = ttt_record(args, world, dev, stream, barrier, max_over_ranks)
+    lion = lion_record(args, world, dev, stream, barrier, max_over_ranks)
+    lm = lm_record(args, world, dev, stream, barrier, max_over_ranks)
+
     # ---- CPU baseline on rank 0 at N=1 ----
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -410,6 +415,9 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         line["seqpar"] = seqpar
         line["single_eval"] = single
+        line["cfg4"] = ttt
+        line["lion"] = lion
+        line["cfg5"] = lm
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
@@ -503,6 +511,114 @@ def seqpar_record(args, world, rank, dev, stream, barrier, max_over_ranks):
             "hbm_gbs_per_gpu": gbs, "hbm_frac_per_gpu": gbs / peak, "peak_kind": kind,
             "parity_ok": bool(err <= 2 ** -7 and ferr < 1e-4), "max_abs_err_vs_unsharded": err,
             "final_state_relerr_vs_unsharded": ferr, "device_status": O.workspace_status()}
+
+
+def tensor_peak():
+    """Sustained cuBLAS bf16 TF/s (the denominator for a kernel timed inside a long step)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        v = d.get("bf16_tflops_sustained") or d.get("bf16_tflops")
+        if v:
+            return float(v), "measured (sustained)"
+    return 1400.0, "fallback (sustained)"
+
+
+def ttt_record(args, world, dev, stream, barrier, max_over_ranks):
+    """BASELINE.json configs[3] per GPU: W_pred MSE TTT with forget-gated Adam,
+    B=4 x S=32768, 2048-token chunks, through the public ttt_wpred_adam (one
+    native call per step: per chunk the forward, the tcgen05 W_pred gradient
+    kernel and the fused reverse adjoint / gradient / Adam kernel).  Both
+    bounds: tensor (the two W_pred products per token, 2 * 2 D^2 flops, against
+    the sustained bf16 peak) and HBM (x read once in bf16 + the fp32 states
+    written once)."""
+    import torch
+    import orthossm_b200 as O
+    Bl, Sl, chunk = 4, 32768, 2048
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(Bl, Sl, D, generator=g, device=dev).to(torch.bfloat16)
+    c = torch.randn(Bl, H, K, HD, generator=g, device=dev) / torch.arange(1, K + 1, device=dev).view(1, 1, K, 1)
+    Wp = torch.randn(D, D, generator=g, device=dev) * 0.02
+    m, v = torch.zeros_like(c), torch.zeros_like(c)
+    lam = torch.tensor(LAMBDA, device=dev)
+    fn = lambda: O.ttt_wpred_adam(x, c, m, v, 0, Wp, lambda_per_head=lam, chunk=chunk)  # noqa: E731
+    steps = max(3, min(args.steps, 20))
+    ms = _timed(fn, steps, args.warmup, stream, barrier, max_over_ranks) / steps
+    flops = Bl * Sl * 2 * 2 * D * D
+    hbm_bytes = Bl * Sl * D * (2 + 4)
+    tpk, tkind = tensor_peak()
+    hpk, hkind = peaks()
+    tf = flops / (ms / 1e3) / 1e12
+    gbs = hbm_bytes / (ms / 1e3) / 1e9
+    return {"workload": "cfg4: W_pred MSE TTT with forget-gated Adam, per GPU B=4 x S=32768, 2048-token chunks "
+                        "(16 sequential chunk steps), W_pred 512x512, bf16 x, fp32 states",
+            "n_gpus": world, "ms_per_step": ms, "tokens_per_s": world * Bl * Sl / (ms / 1e3), "steps": steps,
+            "launches_per_chunk": 5, "chunks": Sl // chunk,
+            "tensor": {"flops_per_step": flops, "achieved_tflops": tf, "peak": tpk, "peak_kind": tkind,
+                       "frac": tf / tpk},
+            "hbm": {"bytes_per_step": hbm_bytes, "achieved_gbs": gbs, "peak": hpk, "peak_kind": hkind,
+                    "frac": gbs / hpk},
+            "bound_note": "16 dependent chunk steps (each chunk's coefficients come from the previous chunk's "
+                          "Adam step), 5 launches each: latency-bound, far from either roofline",
+            "device_status": O.workspace_status()}
+
+
+def lion_record(args, world, dev, stream, barrier, max_over_ranks):
+    """The reference's live op: apply_cheby_rkv_v10 with its chunked Lion TTT
+    (sdpc_kernel.py:2522-2606) at B=2 x S=65536, D=512, 8 heads, degree 8,
+    256-token chunks, seq_threshold=0, the reference's defaults otherwise (LUT
+    evaluation).  HBM bound: x read once (bf16) + the fp32 output written once."""
+    import torch
+    import orthossm_b200 as O
+    Bl, Sl, chunk = 2, 65536, 256
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(Bl, Sl, D, generator=g, device=dev).to(torch.bfloat16)
+    c0 = O.init_chebyshev_coefficients(Bl, H, K, HD, dev)
+    c, mom = c0.clone(), torch.zeros_like(c0)
+
+    def fn():
+        c.copy_(c0)
+        mom.zero_()
+        return O.apply_cheby_rkv_v10(x, c, mom, n_heads=H, chunk_size=chunk, seq_threshold=0)
+
+    steps = max(3, min(args.steps, 10))
+    ms = _timed(fn, steps, args.warmup, stream, barrier, max_over_ranks) / steps
+    hbm_bytes = Bl * Sl * D * (2 + 4)
+    hpk, hkind = peaks()
+    gbs = hbm_bytes / (ms / 1e3) / 1e9
+    return {"workload": "reference live op apply_cheby_rkv_v10 (chunked Lion TTT): per GPU B=2 x S=65536, D=512, "
+                        "8 heads, degree 8, 256-token chunks, seq_threshold=0, LUT evaluation",
+            "n_gpus": world, "ms_per_step": ms, "tokens_per_s": world * Bl * Sl / (ms / 1e3), "steps": steps,
+            "launches_per_step": 1,
+            "hbm": {"bytes_per_step": hbm_bytes, "achieved_gbs": gbs, "peak": hpk, "peak_kind": hkind,
+                    "frac": gbs / hpk},
+            "bound_note": "256 dependent chunk steps per channel (each chunk's Lion update needs the previous "
+                          "chunk's coefficients): latency-bound",
+            "device_status": O.workspace_status()}
+
+
+def lm_record(args, world, dev, stream, barrier, max_over_ranks):
+    """BASELINE.json configs[4] per GPU: the config-5 LM forward (bf16) at
+    B=2 x S=65536 (its cuBLAS GEMMs and flash-attention window are library
+    kernels; the Cheby-RKV path is this package's)."""
+    import torch
+    from orthossm_b200.lm import OrthoLMConfig, OrthoSSMLM, n_params
+    Bl, Sl = 2, 65536
+    cfg = OrthoLMConfig()
+    torch.manual_seed(42)
+    model = OrthoSSMLM(cfg).to(dev, torch.bfloat16).eval()
+    ids = torch.randint(0, cfg.vocab_size, (Bl, Sl), dtype=torch.int64, device=dev)
+    states = model.fresh_states(Bl, dev, generator_seed=7)
+    steps = max(3, min(args.steps, 5))
+    with torch.no_grad():
+        ms = _timed(lambda: model(ids, states), steps, args.warmup, stream, barrier, max_over_ranks) / steps
+    npar = n_params(model)
+    del model
+    return {"workload": f"cfg5: config-5 LM forward, per GPU B={Bl} x S={Sl}, d_model 512, 8 heads, 6 V8 layers "
+                        f"(Cheby-RKV + local attention window 512 + LayerNorm/Linear combine), vocab 32000, "
+                        f"{npar / 1e6:.1f}M parameters (configs[4] says ~72M: the named layers hold 24.3M)",
+            "n_gpus": world, "ms_per_step": ms, "tokens_per_s": world * Bl * Sl / (ms / 1e3), "steps": steps,
+            "dtype": "bf16", "params": npar}
 
 
 def run_lm(args):

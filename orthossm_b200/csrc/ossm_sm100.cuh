@@ -1,7 +1,7 @@
-// sm_100a primitives of the forward kernels: mbarriers, bulk tensor copies
-// (loads into this CTA's own shared memory, stores from it; no multicast),
-// clusters / distributed shared memory, and tensor-memory (TMEM) stores and
-// loads.  Inline PTX only.
+// sm_100a primitives of the forward and TTT kernels: mbarriers, bulk tensor
+// copies (loads into this CTA's own shared memory, stores from it; no
+// multicast), and tensor-memory (TMEM) allocation, stores and loads.  Inline
+// PTX only.
 #pragma once
 
 #include <cuda.h>
@@ -69,57 +69,12 @@ OSSM_DEV void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int 
                ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
                : "memory");
 }
-// 1D bulk copy from this CTA's shared memory into another CTA's of the
-// cluster (cluster addresses of the destination and of its mbarrier), the
-// bytes completing on that mbarrier's transaction count.  16-byte aligned
-// addresses, size a multiple of 16.
-OSSM_DEV void bulk_copy_to_peer(uint32_t cluster_dst, const void* src, uint32_t bytes, uint32_t cluster_bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          cluster_dst),
-      "r"(smem_u32(src)), "r"(bytes), "r"(cluster_bar)
-      : "memory");
-}
 OSSM_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 OSSM_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-OSSM_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 OSSM_DEV void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 OSSM_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// ---------------------------------------------------------------- clusters
-OSSM_DEV uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-OSSM_DEV uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-// Split cluster barrier: every thread of every CTA of the cluster arrives
-// (release: its earlier shared-memory writes, local and remote, become
-// visible) and later waits (acquire) for the phase to complete.
-OSSM_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
-OSSM_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-OSSM_DEV void cluster_sync() {
-  cluster_arrive();
-  cluster_wait();
-}
-// Address of the same shared variable in CTA `rank` of this cluster.
-OSSM_DEV uint32_t map_smem(uint32_t local_addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
-  return r;
-}
-OSSM_DEV void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-OSSM_DEV void st_cluster_v2(uint32_t addr, float2 v) {
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y) : "memory");
-}
 
 // ---------------------------------------------------------------- tcgen05 / TMEM
 OSSM_DEV void tmem_alloc(uint32_t* slot, uint32_t ncols) {  // whole warp
@@ -133,18 +88,8 @@ OSSM_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
 OSSM_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 OSSM_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 32 lanes x 32 columns of 32-bit data: thread i of the warp writes lane
-// (base lane + i), columns col .. col + 31 of taddr, from v[0..31].
-OSSM_DEV void tmem_st32(uint32_t taddr, const float (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]),
-      "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]),
-      "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
-      "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
-      : "memory");
-}
+// 32 lanes x 16 columns of 32-bit data: thread i of the warp writes lane
+// (base lane + i), columns col .. col + 15 of taddr, from v[0..15].
 OSSM_DEV void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
