@@ -593,7 +593,7 @@ def lion_record(args, world, dev, stream, barrier, max_over_ranks):
             "hbm": {"bytes_per_step": hbm_bytes, "achieved_gbs": gbs, "peak": hpk, "peak_kind": hkind,
                     "frac": gbs / hpk},
             "bound_note": "256 dependent chunk steps per channel (each chunk's Lion update needs the previous "
-                          "chunk's coefficients): latency-bound",
+                          "chunk's coefficients): one warp per channel walks them",
             "device_status": O.workspace_status()}
 
 

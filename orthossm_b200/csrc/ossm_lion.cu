@@ -7,16 +7,26 @@
 // updated coefficients feed the next chunk through a host loop.
 //
 // In that computation every channel (b, h, j) is independent: its gradient
-// and Lion step use only its own coefficients, momentum and tokens.  So the
-// chunk loop moves onto the device: a CTA owns a group of channels of one head
-// and walks every chunk of the sequence, keeping coefficients and momentum in
-// shared memory between chunks.  One launch replaces ceil(S/chunk) host-loop
-// iterations, each of which (in the reference) cast x to bf16, cloned the state,
-// allocated fp32 caches, launched, and cast the outputs back.
-//
-// Within a chunk the CTA processes passes of Lp tokens: thread = 4 channels x a
-// run of 8 tokens; runs are combined per channel in shared memory and the pass
-// carry stays in shared memory.
+// and its Lion step use only its own coefficients, momentum and tokens.  The
+// chunk loop therefore moves onto the device, one WARP per channel: the warp
+// walks every chunk of the sequence with the channel's coefficients and Lion
+// momentum in registers (lane k holds c_k and m_k; every lane a broadcast copy
+// of the coefficients).  A chunk is processed in passes of 256 tokens, lane =
+// a run of 8 consecutive tokens:
+//   1. each lane evaluates its 8 tokens and runs the EMA from zero over them;
+//   2. a warp scan of the runs' (decay product, end state) pairs gives each
+//      run its carry-in (and the pass its carry-out) -- no shared-memory fold
+//      and no CTA barrier;
+//   3. each lane forms its final states, the outputs and its share of the
+//      gated-error gradient;
+// and at the chunk's end a butterfly sum over the lanes (a fixed order) gives
+// the gradient, lanes 0..K-1 take the Lion step and broadcast the new
+// coefficients.  A CTA is 8 warps = 8 adjacent channels of one head: x tiles
+// [257 tokens x 8 channels] are loaded coalesced one pass ahead and
+// transposed through shared memory, and the outputs go back the same way, so
+// the only CTA barrier is one per pass.  The serial chain per channel is one
+// pass per 256 tokens (it cannot be parallel across chunks: each chunk's
+// gradient depends on the coefficients the previous chunk's Lion step wrote).
 #include <math.h>
 
 #include "ossm_common.cuh"
@@ -24,14 +34,15 @@
 namespace ossm {
 
 namespace lion {
-constexpr int kNT = 256;
-constexpr int kV = 4;
-constexpr int kR = 8;
-constexpr int kMaxG = 32;  // channels per CTA
+constexpr int kW = 8;                // warps per CTA = channels per CTA
+constexpr int kNT = kW * 32;
+constexpr int kR = 8;                // tokens per lane per pass
+constexpr int kPass = 32 * kR;       // tokens per pass
+constexpr int kRow = kPass + 8;      // transposed tile row (one channel): 257 tokens + pad
 }  // namespace lion
 
 struct LionParams {
-  int B, S, H, HD, K, chunk, G, P, RUNS, Lp, ngroups, D;
+  int B, S, H, HD, K, chunk, D;
   const void* x;
   long long xsb, xss;
   float* coeffs;
@@ -51,13 +62,6 @@ struct LionParams {
 
 // MULTI_SCALE_LAMBDA (sdpc_kernel.py:1416): per-head forget factor of Lion.
 __constant__ float kLionLambda[8] = {0.9995f, 0.9995f, 0.997f, 0.997f, 0.995f, 0.995f, 0.97f, 0.95f};
-
-// x.to(torch.bfloat16) of sdpc_kernel.py:2385, applied on load
-template <typename XT>
-OSSM_DEV float4 load4_bf16_rounded(const XT* p) {
-  const float4 v = ld4(p);
-  return make_float4(bf16_round(v.x), bf16_round(v.y), bf16_round(v.z), bf16_round(v.w));
-}
 
 OSSM_DEV float eval_one(uint32_t ev, const float* lut_s, int K, const float c[8], float xn, float xa,
                         float sgn) {
@@ -93,29 +97,23 @@ OSSM_DEV float eval_one(uint32_t ev, const float* lut_s, int K, const float c[8]
   return fmaf(xn, u1, c[0] - u2);
 }
 
-template <typename XT, typename OT>
-__global__ void __launch_bounds__(lion::kNT, 1) lion_kernel(const LionParams p) {
-  using namespace lion;
-  extern __shared__ float smem[];
-  float* red_s = smem;                 // [RUNS*G][8] gradient partials (8192)
-  float* aggB_s = red_s + 8192;        // [RUNS][G] (1024)
-  float* aggA_s = aggB_s + 1024;       // [RUNS] (128)
-  float* carry_s = aggA_s + 128;       // [G] (32)
-  float* csm = carry_s + 32;           // [8][G] coefficients
-  float* msm = csm + 256;              // [8][G] Lion momentum
-  float* lut_s = msm + 256;            // [8][256]
+// One x element as the reference sees it: x.to(torch.bfloat16) (sdpc_kernel.py:2385).
+OSSM_DEV float x_at(const float* p) { return bf16_round(*p); }
+OSSM_DEV float x_at(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-  const int tid = threadIdx.x;
-  const int grp = blockIdx.x % p.ngroups;
-  const int bh = blockIdx.x / p.ngroups;
-  const int b = bh / p.H;
-  const int h = bh % p.H;
-  const int G = p.G;
-  const int pi = tid % p.P;
-  const int run = tid / p.P;
-  const int jl = pi * kV;             // channel within the group
-  const int jh = grp * G + jl;        // channel within the head
-  const int ch0 = h * p.HD + jh;      // channel within D
+template <typename XT, typename OT>
+__global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
+  using namespace lion;
+  __shared__ float xT[2][kW][kRow];     // x tiles, transposed: [buffer][channel][token]
+  __shared__ float oT[2][kW][kRow];     // output tiles, transposed
+  __shared__ float lut_s[8 * 256];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int ngroups = p.HD / kW;
+  const int grp = blockIdx.x % ngroups, bh = blockIdx.x / ngroups;
+  const int b = bh / p.H, h = bh % p.H;
+  const int j = grp * kW + warp;              // this warp's channel within the head
+  const int ch0 = h * p.HD + grp * kW;        // the CTA's first channel within D
   const uint32_t ev = p.flags & OSSM_EVAL_MASK;
   const int Keff = ev == OSSM_EVAL_CLENSHAW_DEG4 ? min(p.K, 4) : p.K;
 
@@ -128,182 +126,170 @@ __global__ void __launch_bounds__(lion::kNT, 1) lion_kernel(const LionParams p) 
   if (p.gate) lr = lr * __ldg(p.gate + b);
   const float decay = eff - lr * p.wd;
   const float gamma = 0.98f - 0.06f * (float)h / (float)p.H;
+  const float mu = p.mu, oml = 1.f - p.mu;
 
-  const size_t cbase = ((size_t)(b * p.H + h) * p.K) * p.HD + grp * G;
-  for (int i = tid; i < 8 * G; i += kNT) {
-    const int k = i / G, jj = i % G;
-    csm[i] = k < p.K ? p.coeffs[cbase + (size_t)k * p.HD + jj] : 0.f;
-    msm[i] = k < p.K ? p.mom[cbase + (size_t)k * p.HD + jj] : 0.f;
-  }
+  // lane k < K holds coefficient k and its Lion momentum; every lane a copy of all
+  const size_t cidx = ((size_t)(b * p.H + h) * p.K + min(lane, p.K - 1)) * p.HD + j;
+  float my_c = lane < p.K ? p.coeffs[cidx] : 0.f;
+  float my_m = lane < p.K ? p.mom[cidx] : 0.f;
+  float cf[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) cf[k] = __shfl_sync(0xffffffffu, my_c, k);
   if (ev == OSSM_EVAL_LUT)
     for (int i = tid; i < 8 * 256; i += kNT) lut_s[i] = p.lut[i];
-  __syncthreads();
 
   const XT* xb = reinterpret_cast<const XT*>(p.x) + (size_t)b * p.xsb + ch0;
   OT* ob = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + ch0;
-  const float mu = p.mu, oml = 1.f - p.mu;
+  // tile loads: thread r reads token row t0 + r, the CTA's 8 channels; thread
+  // 0 also row t0 + kPass (the next pass's first token)
+  float xr[kW], xe[kW];
+  auto load_rows = [&](int t0) {
+#pragma unroll
+    for (int c = 0; c < kW; ++c) xr[c] = xe[c] = 0.f;
+    if (t0 + tid < p.S) {
+#pragma unroll
+      for (int c = 0; c < kW; ++c) xr[c] = x_at(xb + (size_t)(t0 + tid) * p.xss + c);
+    }
+    if (tid == 0 && t0 + kPass < p.S) {
+#pragma unroll
+      for (int c = 0; c < kW; ++c) xe[c] = x_at(xb + (size_t)(t0 + kPass) * p.xss + c);
+    }
+  };
+  auto store_rows = [&](int bf) {
+#pragma unroll
+    for (int c = 0; c < kW; ++c) xT[bf][c][tid] = xr[c];
+    if (tid == 0) {
+#pragma unroll
+      for (int c = 0; c < kW; ++c) xT[bf][c][kPass] = xe[c];
+    }
+  };
+  static_assert(kNT == kPass, "one thread per tile row");
 
+  int buf = 0;
+  load_rows(0);
+  store_rows(0);
+  __syncthreads();
+
+  float carry = 0.f;  // the EMA state (the final one is written at the end)
   for (int cs = 0; cs < p.S; cs += p.chunk) {
     const int ce = min(cs + p.chunk, p.S);
-    float cf[kV][8];
+    const int Lc = ce - cs;
+    if (p.trace && lane < p.K)  // the chunk's starting coefficients, for the backward
+      p.trace[(size_t)(cs / p.chunk) * ((size_t)p.B * p.H * p.K * p.HD) + cidx] = my_c;
+    float ceff[8];
 #pragma unroll
-    for (int q = 0; q < kV; ++q)
+    for (int k = 0; k < 8; ++k) ceff[k] = k < Keff ? cf[k] : 0.f;
+    float g[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) cf[q][k] = k < Keff ? csm[k * G + jl + q] : 0.f;
-    float g[kV][8];
-#pragma unroll
-    for (int q = 0; q < kV; ++q)
-#pragma unroll
-      for (int k = 0; k < 8; ++k) g[q][k] = 0.f;
-    if (tid < G) carry_s[tid] = 0.f;  // EMA reset per chunk (:2398)
-    if (p.trace && tid < 8 * G) {  // the chunk's starting coefficients, for the backward
-      const int k = tid / G, jj = tid % G;
-      if (k < p.K)
-        p.trace[(size_t)(cs / p.chunk) * ((size_t)p.B * p.H * p.K * p.HD) + cbase + (size_t)k * p.HD + jj] =
-            csm[k * G + jj];
-    }
-    __syncthreads();
+    for (int k = 0; k < 8; ++k) g[k] = 0.f;
+    carry = 0.f;  // EMA reset per chunk (:2398)
 
-    for (int ps = cs; ps < ce; ps += p.Lp) {
-      const int tb = ps + run * kR;
-      // -- phase 1: forward of the run from state 0
-      float sl[kR][kV];
-      float s[kV] = {0.f, 0.f, 0.f, 0.f};
-      float Arun = 1.f;
+    for (int ps = cs; ps < ce; ps += kPass) {
+      // the next pass's rows (next chunk's first pass at a chunk's end) in flight
+      const int nps = ps + kPass < ce ? ps + kPass : ce;
+      load_rows(nps);
+      const int tb = ps + lane * kR;
+      // -- 1: the lane's 8 tokens from state 0; xn of 9 tokens (the 9th is the
+      //       next run's first, for the prediction error of the last)
+      float sl[kR], xn[kR + 1];
+      float s = 0.f, Arun = 1.f;
 #pragma unroll
-      for (int r = 0; r < kR; ++r) {
-        const int t = tb + r;
-        const bool valid = t < ce;
-        float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid) xv = load4_bf16_rounded(xb + (size_t)t * p.xss);
-        const float xa4[kV] = {xv.x, xv.y, xv.z, xv.w};
-        float u[kV];
-#pragma unroll
-        for (int q = 0; q < kV; ++q) {
-          float xa, sg;
-          const float xn = softsign<true>(xa4[q], false, xa, sg);
-          const float y = eval_one(ev, lut_s, p.K, cf[q], xn, xa, sg) * gamma;
+      for (int r = 0; r <= kR; ++r) {
+        const float xv = xT[buf][warp][lane * kR + r];
+        float xa, sg;
+        xn[r] = softsign<true>(xv, false, xa, sg);
+        if (r < kR) {
+          const bool valid = tb + r < ce;
+          const float y = eval_one(ev, lut_s, p.K, ceff, xn[r], xa, sg) * gamma;
           const float yc = fminf(fmaxf(y, -4.f), 4.f);
-          u[q] = (xa4[q] != xa4[q] || !valid) ? 0.f : tanhf(yc);
-          if (valid) s[q] = fmaf(mu, s[q], oml * u[q]);
-          sl[r][q] = s[q];
-        }
-        if (valid) Arun *= mu;
-        if (p.tanh_out && valid)
-          st4(p.tanh_out + (size_t)b * p.osb + (size_t)t * p.oss + ch0, make_float4(u[0], u[1], u[2], u[3]));
-      }
-      // -- phase 2: combine runs per channel, carry from the previous pass
-#pragma unroll
-      for (int q = 0; q < kV; ++q) aggB_s[run * G + jl + q] = s[q];
-      if (pi == 0) aggA_s[run] = Arun;
-      __syncthreads();
-      if (tid < G) {
-        float Bv = carry_s[tid];
-        for (int q = 0; q < p.RUNS; ++q) {
-          const float bq = aggB_s[q * G + tid];
-          aggB_s[q * G + tid] = Bv;
-          Bv = fmaf(aggA_s[q], Bv, bq);
-        }
-        carry_s[tid] = Bv;
-      }
-      __syncthreads();
-      // -- phase 3: final states, outputs, TTT gradient
-      float rc[kV];
-#pragma unroll
-      for (int q = 0; q < kV; ++q) rc[q] = aggB_s[run * G + jl + q];
-      float xn_t[kV];
-      if (tb < ce) {
-        const float4 xv = load4_bf16_rounded(xb + (size_t)tb * p.xss);
-        const float xa4[kV] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-        for (int q = 0; q < kV; ++q) {
-          float xa, sg;
-          xn_t[q] = softsign<true>(xa4[q], false, xa, sg);
+          const float u = (xv != xv || !valid) ? 0.f : tanhf(yc);
+          if (valid) {
+            s = fmaf(mu, s, oml * u);
+            Arun *= mu;
+          }
+          sl[r] = s;
+          if (p.tanh_out && valid)
+            p.tanh_out[(size_t)b * p.osb + (size_t)(tb + r) * p.oss + ch0 + warp] = u;
         }
       }
+      // -- 2: carries of the runs: inclusive scan of (A, B), then shift by one
+      float A = Arun, Bs = s;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float Ao = __shfl_up_sync(0xffffffffu, A, off), Bo = __shfl_up_sync(0xffffffffu, Bs, off);
+        if (lane >= off) {
+          Bs = fmaf(A, Bo, Bs);
+          A *= Ao;
+        }
+      }
+      const float Ae = __shfl_up_sync(0xffffffffu, A, 1), Be = __shfl_up_sync(0xffffffffu, Bs, 1);
+      const float cin = lane == 0 ? carry : fmaf(Ae, carry, Be);
+      carry = fmaf(__shfl_sync(0xffffffffu, A, 31), carry, __shfl_sync(0xffffffffu, Bs, 31));
+      // -- 3: final states, outputs, the gated-error gradient (:2141-2169)
       float Acum = 1.f;
 #pragma unroll
       for (int r = 0; r < kR; ++r) {
         const int t = tb + r;
         if (t < ce) {
           Acum *= mu;
-          float sf[kV];
+          const float sf = clamp1(fmaf(Acum, cin, sl[r]));
+          oT[buf][warp][lane * kR + r] = sizeof(OT) == 4 ? bf16_round(sf) : sf;
+          // e = xn_{t+1} - s_t, weight sigmoid(3|e|), Chebyshev basis of xn_t
+          const float e = t + 1 < ce ? xn[r + 1] - sf : 0.f;
+          const float w = 1.0f / (1.0f + expf(-3.0f * fabsf(e)));
+          const float gv = e * w;
+          const float xq = xn[r];
+          float T0 = 1.f, T1 = xq;
+          g[0] = fmaf(gv, T0, g[0]);
+          g[1] = fmaf(gv, T1, g[1]);
 #pragma unroll
-          for (int q = 0; q < kV; ++q) sf[q] = clamp1(fmaf(Acum, rc[q], sl[r][q]));
-          if (sizeof(OT) == 4)
-            st4(ob + (size_t)t * p.oss,
-                make_float4(bf16_round(sf[0]), bf16_round(sf[1]), bf16_round(sf[2]), bf16_round(sf[3])));
-          else
-            st4(ob + (size_t)t * p.oss, make_float4(sf[0], sf[1], sf[2], sf[3]));
-          const bool has_next = t + 1 < ce;
-          float xn_n[kV] = {0.f, 0.f, 0.f, 0.f};
-          if (has_next) {
-            const float4 xv = load4_bf16_rounded(xb + (size_t)(t + 1) * p.xss);
-            const float xa4[kV] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-            for (int q = 0; q < kV; ++q) {
-              float xa, sg;
-              xn_n[q] = softsign<true>(xa4[q], false, xa, sg);
-            }
-          }
-          // e = xn_{t+1} - s_t, weight sigmoid(3|e|), Chebyshev basis of xn_t (:2141-2169)
-#pragma unroll
-          for (int q = 0; q < kV; ++q) {
-            const float e = has_next ? xn_n[q] - sf[q] : 0.f;
-            const float w = 1.0f / (1.0f + expf(-3.0f * fabsf(e)));
-            const float gv = e * w;
-            const float xq = xn_t[q];
-            float T0 = 1.f, T1 = xq;
-            g[q][0] = fmaf(gv, T0, g[q][0]);
-            g[q][1] = fmaf(gv, T1, g[q][1]);
-#pragma unroll
-            for (int k = 2; k < 8; ++k) {
-              const float T2 = 2.0f * xq * T1 - T0;
-              g[q][k] = fmaf(gv, T2, g[q][k]);
-              T0 = T1;
-              T1 = T2;
-            }
-            xn_t[q] = xn_n[q];
+          for (int k = 2; k < 8; ++k) {
+            const float T2 = 2.0f * xq * T1 - T0;
+            g[k] = fmaf(gv, T2, g[k]);
+            T0 = T1;
+            T1 = T2;
           }
         }
       }
-      __syncthreads();  // aggB_s / carry reuse in the next pass
-    }
-
-    // -- chunk end: reduce the gradient over runs, Lion (:2179-2287)
+      store_rows(buf ^ 1);
+      __syncthreads();  // outputs of this pass and x of the next are in place
+      // coalesced output rows: thread r writes token ps + r, the CTA's 8 channels
+      if (tid < kPass && ps + tid < ce) {
+        OT* op = ob + (size_t)(ps + tid) * p.oss;
 #pragma unroll
-    for (int q = 0; q < kV; ++q)
-#pragma unroll
-      for (int k = 0; k < 8; ++k) red_s[(run * G + jl + q) * 8 + k] = g[q][k];
-    __syncthreads();
-    if (tid < G * 8) {
-      const int jj = tid >> 3, k = tid & 7;
-      if (k < p.K) {
-        float gs = 0.f;
-        for (int q = 0; q < p.RUNS; ++q) gs += red_s[(q * G + jj) * 8 + k];
-        const int Lc = ce - cs;
-        // the reference divides by Lc - 1 (NaN for a 1-token chunk); a
-        // 1-token chunk has no prediction pair and contributes no gradient.
-        const float gr = Lc > 1 ? gs * (1.0f / (float)(Lc - 1)) : 0.f;
-        const float m = msm[k * G + jj];
-        const float c = csm[k * G + jj];
-        const float interp = p.beta1 * m + (1.0f - p.beta1) * gr;
-        const float sgn = interp > 0.f ? 1.f : (interp < 0.f ? -1.f : 0.f);
-        msm[k * G + jj] = p.beta2 * m + (1.0f - p.beta2) * gr;
-        csm[k * G + jj] = decay * c + lr * p.ss[k] * sgn;
+        for (int c = 0; c < kW; c += 4)
+          st4(op + c, make_float4(oT[buf][c][tid], oT[buf][c + 1][tid], oT[buf][c + 2][tid], oT[buf][c + 3][tid]));
       }
+      buf ^= 1;
     }
-    __syncthreads();
+
+    // -- chunk end: the gradient over the lanes (butterfly, fixed order), Lion (:2179-2287)
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) g[k] += __shfl_xor_sync(0xffffffffu, g[k], off);
+    float gk = g[0];
+#pragma unroll
+    for (int k = 1; k < 8; ++k)
+      if (lane == k) gk = g[k];
+    if (lane < p.K) {
+      // the reference divides by Lc - 1 (NaN for a 1-token chunk); a 1-token
+      // chunk has no prediction pair and contributes no gradient.
+      const float gr = Lc > 1 ? gk * (1.0f / (float)(Lc - 1)) : 0.f;
+      const float interp = p.beta1 * my_m + (1.0f - p.beta1) * gr;
+      const float sgn = interp > 0.f ? 1.f : (interp < 0.f ? -1.f : 0.f);
+      my_m = p.beta2 * my_m + (1.0f - p.beta2) * gr;
+      my_c = decay * my_c + lr * p.ss[lane] * sgn;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) cf[k] = __shfl_sync(0xffffffffu, my_c, k);
   }
 
-  for (int i = tid; i < 8 * G; i += kNT) {
-    const int k = i / G, jj = i % G;
-    if (k < p.K) {
-      p.coeffs[cbase + (size_t)k * p.HD + jj] = csm[i];
-      p.mom[cbase + (size_t)k * p.HD + jj] = msm[i];
-    }
+  if (lane < p.K) {
+    p.coeffs[cidx] = my_c;
+    p.mom[cidx] = my_m;
   }
-  if (p.fin && tid < G) p.fin[(size_t)b * p.D + h * p.HD + grp * G + tid] = carry_s[tid];
+  if (p.fin && lane == 0) p.fin[(size_t)b * p.D + h * p.HD + j] = carry;
 }
 
 }  // namespace ossm
@@ -315,10 +301,7 @@ bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 
 template <typename XT, typename OT>
 cudaError_t launch_lion(const LionParams& p, int grid, cudaStream_t st) {
-  const size_t smem = (8192 + 1024 + 128 + 32 + 256 + 256 + 2048) * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(lion_kernel<XT, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  lion_kernel<XT, OT><<<grid, lion::kNT, smem, st>>>(p);
+  lion_kernel<XT, OT><<<grid, lion::kNT, 0, st>>>(p);
   return cudaGetLastError();
 }
 }  // namespace
@@ -346,11 +329,6 @@ extern "C" int ossm_cheby_rkv_lion(const ossm_lion_args* a, ossm_stream_t stream
   p.HD = a->head_dim;
   p.K = a->degree;
   p.chunk = a->chunk;
-  p.G = a->head_dim < lion::kMaxG ? a->head_dim : lion::kMaxG;
-  p.P = p.G / lion::kV;
-  p.RUNS = lion::kNT / p.P;
-  p.Lp = p.RUNS * lion::kR;
-  p.ngroups = a->head_dim / p.G;
   p.D = (int)D;
   p.x = a->x;
   p.xsb = a->x_stride_b;
@@ -373,7 +351,7 @@ extern "C" int ossm_cheby_rkv_lion(const ossm_lion_args* a, ossm_stream_t stream
   p.fin = a->final_state;
   p.flags = a->flags;
   p.trace = a->coeff_trace;
-  const long long grid = (long long)a->B * a->H * p.ngroups;
+  const long long grid = (long long)a->B * a->H * (a->head_dim / lion::kW);
   if (grid > 0x7fffffffLL) return OSSM_EINVAL;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
