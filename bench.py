@@ -24,6 +24,14 @@ configs[4]; orthossm_b200.lm): per GPU B=2 x S=65536 token ids, 6 V8 layers
 of d_model 512, vocab 32000, bf16.  Its JSON line reports tokens/s of the
 forward (value), of ids-in / loss-out through the model (e2e), and the share of
 the step spent in this package's Cheby-EMA kernels.
+--workload lion times the reference's live op (apply_cheby_rkv_v10 with its
+chunked Lion TTT) at B=2 x S=65536 per GPU.
+
+The default line also carries sub-records for those workloads (seqpar, cfg4,
+lion, cfg5) and for the opt-in single-evaluation forward (single_eval), each
+timed with CUDA events on the bench's stream, max over ranks.
+--profile-once (cfg2, cfg3, cfg4, lion) runs 3 warm-up steps and one more,
+nothing timed: the command that ncu captures.
 """
 from __future__ import annotations
 
@@ -60,7 +68,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--soak-s", type=float, default=1.5, help="loaded seconds sampled for clocks before timing")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5", "lion"], default="cfg2")
     ap.add_argument("--profile-once", action="store_true",
                     help="3 warm-up steps + 1 step, nothing else: for ncu")
     return ap.parse_args()
@@ -864,6 +872,16 @@ def run_cfg4(args):
     lam = torch.tensor(LAMBDA, device=dev)
     stream = torch.cuda.Stream(dev)
     fn = lambda: O.ttt_wpred_adam(x, c, m, v, 0, Wp, lambda_per_head=lam, chunk=chunk)  # noqa: E731
+    if args.profile_once:  # 3 warm-up calls + the profiled one, nothing timed
+        with torch.cuda.stream(stream):
+            for _ in range(4):
+                fn()
+        torch.cuda.synchronize()
+        if rank == 0:
+            print("profile-once done, status", O.workspace_status())
+        if world > 1:
+            dist.destroy_process_group()
+        return
     try:
         gid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     except Exception:
@@ -895,6 +913,42 @@ def run_cfg4(args):
         dist.destroy_process_group()
 
 
+def run_lion(args):
+    """The reference's live op (apply_cheby_rkv_v10 with its Lion TTT) as the
+    main line: the `lion` record's workload, per GPU, weak scaling."""
+    import torch
+    import torch.distributed as dist
+    import orthossm_b200 as O
+    world, rank, local, dev, mor, barrier = _dist_setup()
+    stream = torch.cuda.Stream(dev)
+    if args.profile_once:  # 3 warm-up calls + the profiled one, nothing timed
+        g = torch.Generator(device=dev).manual_seed(11)
+        x = torch.randn(2, 65536, D, generator=g, device=dev).to(torch.bfloat16)
+        c0 = O.init_chebyshev_coefficients(2, H, K, HD, dev)
+        with torch.cuda.stream(stream):
+            for _ in range(4):
+                O.apply_cheby_rkv_v10(x, c0.clone(), torch.zeros_like(c0), n_heads=H, chunk_size=256,
+                                      seq_threshold=0)
+        torch.cuda.synchronize()
+        if rank == 0:
+            print("profile-once done")
+    else:
+        rec = lion_record(args, world, dev, stream, barrier, mor)
+        if rank == 0:
+            print(json.dumps({
+                "metric": "tokens/sec", "value": rec["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+                "steps": rec["steps"], "warmup": max(args.warmup, 3), "ms_per_step": rec["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 compute (bf16 x, fp32 out rounded to bf16 as the reference does)",
+                "data": "synthetic (seeded)",
+                "config": {"workload": rec["workload"], "global_batch": 2 * world, "seq_len": 65536,
+                           "parallelism": f"batch-sharded x{world}"},
+                "roofline": dict(rec["hbm"], bound="hbm", unit="GB/s", achieved=rec["hbm"]["achieved_gbs"]),
+                "device_status": rec["device_status"]}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -905,6 +959,8 @@ def main():
         run_cfg3(args)
     elif args.workload == "cfg4":
         run_cfg4(args)
+    elif args.workload == "lion":
+        run_lion(args)
     else:
         run_ours(args)
 

@@ -38,7 +38,11 @@ constexpr int kW = 8;                // warps per CTA = channels per CTA
 constexpr int kNT = kW * 32;
 constexpr int kR = 8;                // tokens per lane per pass
 constexpr int kPass = 32 * kR;       // tokens per pass
-constexpr int kRow = kPass + 8;      // transposed tile row (one channel): 257 tokens + pad
+// A channel's tile row holds token t of the pass at (t % 8) * 33 + t / 8
+// (lane-major: lane l reads its r-th token at r * 33 + l, no bank conflicts),
+// the 257th token (the next pass's first) at 8 * 33.
+constexpr int kRow = 8 * 33 + 1;
+OSSM_DEV int slot(int t) { return t < kPass ? (t & 7) * 33 + (t >> 3) : 8 * 33; }
 }  // namespace lion
 
 struct LionParams {
@@ -63,7 +67,9 @@ struct LionParams {
 // MULTI_SCALE_LAMBDA (sdpc_kernel.py:1416): per-head forget factor of Lion.
 __constant__ float kLionLambda[8] = {0.9995f, 0.9995f, 0.997f, 0.997f, 0.995f, 0.995f, 0.97f, 0.95f};
 
-OSSM_DEV float eval_one(uint32_t ev, const float* lut_s, int K, const float c[8], float xn, float xa,
+// lut2[k * 256 + i] = (T_k(i / 255), T_k((i + 1) / 255)): both interpolation
+// ends in one 8-byte shared load.
+OSSM_DEV float eval_one(uint32_t ev, const float2* lut2, int K, const float c[8], float xn, float xa,
                         float sgn) {
   if (ev == OSSM_EVAL_LUT) {
     // sdpc_kernel.py:2030-2069
@@ -75,8 +81,8 @@ OSSM_DEV float eval_one(uint32_t ev, const float* lut_s, int K, const float c[8]
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       if (k < K) {
-        const float ta = lut_s[k * 256 + i0];
-        const float tb = lut_s[k * 256 + i0 + 1];
+        const float2 tt = lut2[k * 256 + i0];
+        const float ta = tt.x, tb = tt.y;
         float v = c[k] * (ta + fr * (tb - ta));
         if (k & 1) v *= sgn;
         y += v;
@@ -106,7 +112,7 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
   using namespace lion;
   __shared__ float xT[2][kW][kRow];     // x tiles, transposed: [buffer][channel][token]
   __shared__ float oT[2][kW][kRow];     // output tiles, transposed
-  __shared__ float lut_s[8 * 256];
+  extern __shared__ float2 lut2[];       // [8 * 256] (LUT evaluation only)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int ngroups = p.HD / kW;
@@ -136,7 +142,7 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
 #pragma unroll
   for (int k = 0; k < 8; ++k) cf[k] = __shfl_sync(0xffffffffu, my_c, k);
   if (ev == OSSM_EVAL_LUT)
-    for (int i = tid; i < 8 * 256; i += kNT) lut_s[i] = p.lut[i];
+    for (int i = tid; i < 8 * 256; i += kNT) lut2[i] = make_float2(p.lut[i], (i & 255) < 255 ? p.lut[i + 1] : 0.f);
 
   const XT* xb = reinterpret_cast<const XT*>(p.x) + (size_t)b * p.xsb + ch0;
   OT* ob = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + ch0;
@@ -157,10 +163,10 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
   };
   auto store_rows = [&](int bf) {
 #pragma unroll
-    for (int c = 0; c < kW; ++c) xT[bf][c][tid] = xr[c];
+    for (int c = 0; c < kW; ++c) xT[bf][c][slot(tid)] = xr[c];
     if (tid == 0) {
 #pragma unroll
-      for (int c = 0; c < kW; ++c) xT[bf][c][kPass] = xe[c];
+      for (int c = 0; c < kW; ++c) xT[bf][c][slot(kPass)] = xe[c];
     }
   };
   static_assert(kNT == kPass, "one thread per tile row");
@@ -195,12 +201,12 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
       float s = 0.f, Arun = 1.f;
 #pragma unroll
       for (int r = 0; r <= kR; ++r) {
-        const float xv = xT[buf][warp][lane * kR + r];
+        const float xv = xT[buf][warp][r < kR ? r * 33 + lane : slot(lane * kR + kR)];
         float xa, sg;
         xn[r] = softsign<true>(xv, false, xa, sg);
         if (r < kR) {
           const bool valid = tb + r < ce;
-          const float y = eval_one(ev, lut_s, p.K, ceff, xn[r], xa, sg) * gamma;
+          const float y = eval_one(ev, lut2, p.K, ceff, xn[r], xa, sg) * gamma;
           const float yc = fminf(fmaxf(y, -4.f), 4.f);
           const float u = (xv != xv || !valid) ? 0.f : tanhf(yc);
           if (valid) {
@@ -233,10 +239,10 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
         if (t < ce) {
           Acum *= mu;
           const float sf = clamp1(fmaf(Acum, cin, sl[r]));
-          oT[buf][warp][lane * kR + r] = sizeof(OT) == 4 ? bf16_round(sf) : sf;
+          oT[buf][warp][r * 33 + lane] = sizeof(OT) == 4 ? bf16_round(sf) : sf;
           // e = xn_{t+1} - s_t, weight sigmoid(3|e|), Chebyshev basis of xn_t
           const float e = t + 1 < ce ? xn[r + 1] - sf : 0.f;
-          const float w = 1.0f / (1.0f + expf(-3.0f * fabsf(e)));
+          const float w = __frcp_rn(1.0f + __expf(-3.0f * fabsf(e)));
           const float gv = e * w;
           const float xq = xn[r];
           float T0 = 1.f, T1 = xq;
@@ -258,7 +264,8 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
         OT* op = ob + (size_t)(ps + tid) * p.oss;
 #pragma unroll
         for (int c = 0; c < kW; c += 4)
-          st4(op + c, make_float4(oT[buf][c][tid], oT[buf][c + 1][tid], oT[buf][c + 2][tid], oT[buf][c + 3][tid]));
+          st4(op + c, make_float4(oT[buf][c][slot(tid)], oT[buf][c + 1][slot(tid)], oT[buf][c + 2][slot(tid)],
+                                  oT[buf][c + 3][slot(tid)]));
       }
       buf ^= 1;
     }
@@ -301,7 +308,10 @@ bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 
 template <typename XT, typename OT>
 cudaError_t launch_lion(const LionParams& p, int grid, cudaStream_t st) {
-  lion_kernel<XT, OT><<<grid, lion::kNT, 0, st>>>(p);
+  const size_t dyn = (p.flags & OSSM_EVAL_MASK) == OSSM_EVAL_LUT ? 8 * 256 * sizeof(float2) : 0;
+  cudaError_t e = cudaFuncSetAttribute(lion_kernel<XT, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+  if (e != cudaSuccess) return e;
+  lion_kernel<XT, OT><<<grid, lion::kNT, dyn, st>>>(p);
   return cudaGetLastError();
 }
 }  // namespace
