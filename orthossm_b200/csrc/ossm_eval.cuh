@@ -161,6 +161,31 @@ OSSM_DEV float2 ema_chunk_exact(float2 s, const float2* lam, bool first, const f
   return s;
 }
 
+// The same two loops, handing each token's u to U(t, u) as well (the
+// aggregate pass parks u for the output pass).
+template <bool PRECISE, bool EXACT, typename RawF, typename UF>
+OSSM_DEV float2 ema_chunk_u(float2 s, const float2* lam, bool first, const float2 (&m)[8], float gamma, RawF raw,
+                            UF uf) {
+#pragma unroll
+  for (int t = 0; t < kL; ++t) {
+    const float2 u = eval_u<PRECISE, EXACT>(raw(t), m, gamma);
+    uf(t, u);
+    s = ema_step(s, lam[t], u, t == 0 && first);
+  }
+  return s;
+}
+template <bool PRECISE, typename RawF, typename UF>
+OSSM_DEV float2 ema_chunk_u_exact(float2 s, const float2* lam, bool first, const float2 (&m)[8], float gamma,
+                                  RawF raw, UF uf) {
+#pragma unroll 1
+  for (int t = 0; t < kL; ++t) {
+    const float2 u = eval_u<PRECISE, true>(raw(t), m, gamma);
+    uf(t, u);
+    s = ema_step(s, lam[t], u, t == 0 && first);
+  }
+  return s;
+}
+
 OSSM_DEV void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])

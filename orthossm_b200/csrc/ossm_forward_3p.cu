@@ -19,7 +19,10 @@
 //                    the blocks of chains longer than one block.
 //   p3_out_kernel    one CTA per (b, chunk), warp = head: re-reads x, evaluates
 //                    u again and runs the EMA from the chunk's carry, writing
-//                    each output as it is produced.
+//                    each output as it is produced.  For fp32 outputs that fit
+//                    in half of L2, the aggregate pass parks u in the output
+//                    rows instead and p3_outu_kernel reads it back (no second
+//                    evaluation).
 //
 // Every launch streams with high occupancy and no inter-CTA waits; the price is
 // a second evaluation and a second read of x.  Results are bitwise
@@ -141,6 +144,9 @@ struct Params {
   float* tot_E;           // [B*H][64] shard end states from a zero state (or NULL)
   const float* carry_in;  // [B][D] state entering the shard (or NULL: zero / init_state)
   float* shard_carry;     // [B][D] workspace slot where a sharded call folds carry_in
+  // 1: the aggregate pass parks u (fp32) in the fp32 output buffer and the
+  // output pass reads it back instead of evaluating again
+  int uc;
 };
 
 // w = hi + lo with hi = bf16(w) and lo = bf16(w - hi), for a pair of weights,
@@ -202,7 +208,7 @@ OSSM_DEV float lam_token(const Params& p, const float* lam_tok, int b, int tg, i
 // ---------------------------------------------------------------------------
 // pass 1: chunk aggregates
 // ---------------------------------------------------------------------------
-template <bool GATE, bool PRECISE>
+template <bool GATE, bool PRECISE, bool UC>
 __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
   using namespace sm100;
   extern __shared__ uint8_t smem_raw[];
@@ -294,13 +300,23 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
 #pragma unroll
   for (int k = 0; k < 8; ++k) roff[k] = (uint32_t)((((lane >> 2) ^ k) << 4) + (lane & 3) * 4);
   auto raw = [&](int t) { return *reinterpret_cast<const uint32_t*>(xs + roff[t & 7] + t * 128); };
-  auto none = [](int, float2) {};
-  s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, none);
-  if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y)) {  // NaN / inf inputs: the reference's semantics
-    auto raw_t = [&](int t) {
-      return *reinterpret_cast<const uint32_t*>(xs + box_off(t, lane >> 2) + (lane & 3) * 4);
+  auto raw_t = [&](int t) {
+    return *reinterpret_cast<const uint32_t*>(xs + box_off(t, lane >> 2) + (lane & 3) * 4);
+  };
+  if (UC) {  // park each u in the fp32 output row it will become (tokens past the end have no row)
+    float* uo = static_cast<float*>(p.out) + (size_t)b * p.osb + (size_t)t0 * p.oss + h * kHD + j0;
+    const int nt = min(kL, p.S - t0);
+    auto put = [&](int t, float2 u) {
+      if (t < nt) *reinterpret_cast<float2*>(uo + (size_t)t * p.oss) = u;
     };
-    s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, first, cm, gamma, raw_t, none);
+    s = ema_chunk_u<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, put);
+    if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y))  // NaN / inf inputs: the reference's semantics
+      s = ema_chunk_u_exact<PRECISE>(s_in, lam_s + h * kL, first, cm, gamma, raw_t, put);
+  } else {
+    auto none = [](int, float2) {};
+    s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, none);
+    if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y))  // NaN / inf inputs: the reference's semantics
+      s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, first, cm, gamma, raw_t, none);
   }
   const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
   *reinterpret_cast<float2*>(p.agg + n * kHD + j0) = s;
@@ -529,9 +545,81 @@ __global__ void __launch_bounds__(kNT, PRECISE ? 3 : 4) p3_out_kernel(const Para
     *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) = make_float2(clamp1(s.x), clamp1(s.y));
 }
 
-template <bool GATE, bool PRECISE>
+// pass 3 of an fp32-output forward from the u the aggregate pass parked in the
+// output buffer: no second evaluation (the precise path's tanhf and IEEE
+// division are most of its cost).  Each lane reads its 32 u pairs (one
+// coalesced 256-byte row per warp and token), runs the EMA from the chunk's
+// carry and overwrites them with the outputs: the arithmetic of the
+// re-evaluating pass on the same u, so the outputs are bitwise equal.
+__global__ void __launch_bounds__(kNT, 4) p3_outu_kernel(const Params p, const float* lam_tok) {
+  __shared__ float2 lam_s[kH * kL];
+  const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
+  const int j0 = lane * 2, ch0 = h * kHD + j0;
+  const int c = (int)(blockIdx.x / p.B), b = (int)(blockIdx.x % p.B);
+  const int t0 = c * kL, nt = min(kL, p.S - t0);
+  const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
+  float* op = static_cast<float*>(p.out) + (size_t)b * p.osb + (size_t)t0 * p.oss + ch0;
+  // the parked u of the first 16 tokens go out first: their latency overlaps
+  // the carry and decay loads (16 at a time keeps the fp32 case in registers)
+  constexpr int kHalf = kL / 2;
+  float2 u[kHalf];
+  auto load_u = [&](int t0h) {
+#pragma unroll
+    for (int q = 0; q < kHalf; ++q) {
+      const int t = t0h + q;
+      u[q] = t < nt ? *reinterpret_cast<const float2*>(op + (size_t)t * p.oss) : make_float2(0.f, 0.f);
+    }
+  };
+  load_u(0);
+  const bool first = c == 0 && p.starts_seq;
+  float2 X;
+  if (first) {
+    X = p.init ? __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + ch0)) : make_float2(0.f, 0.f);
+  } else {
+    X = c == 0 ? make_float2(0.f, 0.f) : *reinterpret_cast<const float2*>(p.carry + n * kHD + j0);
+    const int blk = c / kBlk;
+    if (blk > 0 || p.carry_in) {  // the state entering the chunk's block, decayed to this chunk
+      const size_t k = (size_t)(b * kH + h) * p.nblk + blk;
+      float2 Y = make_float2(0.f, 0.f);
+      float Pb = 1.f;
+      if (blk > 0) {
+        Y = *reinterpret_cast<const float2*>(p.blk_X + k * kHD + j0);
+        Pb = p.blk_P[k];
+      }
+      if (p.carry_in) {  // the state entering the shard
+        const float2 ci = __ldg(reinterpret_cast<const float2*>(p.carry_in + (size_t)b * kD + ch0));
+        Y = make_float2(fmaf(Pb, ci.x, Y.x), fmaf(Pb, ci.y, Y.y));
+      }
+      const float Pn = c == 0 ? 1.f : p.P[n];
+      X = make_float2(fmaf(Pn, Y.x, X.x), fmaf(Pn, Y.y, X.y));
+    }
+  }
+  const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
+  const float lam = lam_token(p, lam_tok, b, t0 + lane, h, lam_base);
+  lam_s[h * kL + lane] = make_float2(lam, 1.f - lam);
+  __syncwarp();
+  const float2* lm = lam_s + h * kL;
+  float2 s = X;
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    if (hf == 1) load_u(kHalf);
+#pragma unroll
+    for (int q = 0; q < kHalf; ++q) {
+      const int t = hf * kHalf + q;
+      if (t < nt) {
+        s = ema_step(s, lm[t], u[q], t == 0 && first);
+        st2(op + (size_t)t * p.oss, make_float2(clamp1(s.x), clamp1(s.y)));
+      }
+    }
+  }
+  // decays are 1 past the end, so the chunk's last state is the sequence's final state
+  if (p.fin && t0 + kL >= p.S)
+    *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) = make_float2(clamp1(s.x), clamp1(s.y));
+}
+
+template <bool GATE, bool PRECISE, bool UC>
 cudaError_t launch_agg(const CUtensorMap& mx, const Params& p, cudaStream_t st) {
-  auto kern = p3_agg_kernel<GATE, PRECISE>;
+  auto kern = p3_agg_kernel<GATE, PRECISE, UC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAggSmem);
   if (e != cudaSuccess) return e;
   kern<<<p.B * p.nchunks, kNT, kAggSmem, st>>>(mx, p);
@@ -702,8 +790,30 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
   p.tot_A = nullptr;
   p.tot_E = nullptr;
   p.carry_in = nullptr;
+  p.uc = 0;
   if ((long long)a->B * p.nchunks > 0x7fffffffLL || (long long)a->B * kH * p.nblk > 0x7fffffffLL) return OSSM_EINVAL;
   return OSSM_OK;
+}
+
+// Whether the aggregate pass parks u in the output buffer for the output pass:
+// fp32 outputs only (u fits the output row exactly), whole-forward launches
+// only (the sharded entry points may be handed another output buffer for
+// their second call), not when x and out overlap in memory (the parked u
+// would overwrite x another chunk still reads), and while the outputs fit in
+// half of L2, so the parked u is read back from L2.  Measured: the TTT step
+// of BASELINE.json configs[3] (16 forwards of 4 x 2048 tokens with fp32
+// states) went from 1.50 to 1.38 ms; for bf16 outputs, u parked as fp16 made
+// the config-2 step slower (122.8 -> 135.7 us): the extra 134 MB of writes
+// left L2 before the output pass read them.
+int p3_uc_mode(const ossm_fwd_args* a) {
+  if (a->out_dtype != OSSM_F32) return 0;
+  const size_t D = (size_t)a->H * a->head_dim;
+  const char* x0 = static_cast<const char*>(a->x);
+  const char* x1 = x0 + ((size_t)(a->B - 1) * a->x_stride_b + (size_t)(a->S - 1) * a->x_stride_s + D) * 2;
+  const char* o0 = static_cast<const char*>(a->out);
+  const char* o1 = o0 + ((size_t)(a->B - 1) * a->out_stride_b + (size_t)(a->S - 1) * a->out_stride_s + D) * 4;
+  if (o0 < x1 && x0 < o1) return 0;
+  return (size_t)a->B * a->S * D * 4 <= (64u << 20) ? 1 : 0;
 }
 
 // pass 1: aggregates
@@ -723,10 +833,12 @@ int p3_aggregates(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) 
       p3_prep_kernel<true, false><<<nprep, 32, 0, st>>>(p);
   }
   cudaError_t e;
-  if (precise)
-    e = gate ? launch_agg<true, true>(mx, p, st) : launch_agg<false, true>(mx, p, st);
+  if (p.uc)
+    e = gate ? launch_agg<true, true, true>(mx, p, st) : launch_agg<false, true, true>(mx, p, st);
+  else if (precise)
+    e = gate ? launch_agg<true, true, false>(mx, p, st) : launch_agg<false, true, false>(mx, p, st);
   else
-    e = gate ? launch_agg<true, false>(mx, p, st) : launch_agg<false, false>(mx, p, st);
+    e = gate ? launch_agg<true, false, false>(mx, p, st) : launch_agg<false, false, false>(mx, p, st);
   return e == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
 }
 
@@ -751,7 +863,10 @@ int p3_back(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
   const bool precise = (a->out_dtype == OSSM_F32) || (a->flags & OSSM_F_PRECISE);
   const float* lam_tok = gate ? p.lam_ws : a->lam_tok;
   cudaError_t e;
-  if (a->out_dtype == OSSM_F32)
+  if (p.uc) {
+    p3_outu_kernel<<<p.B * p.nchunks, kNT, 0, st>>>(p, lam_tok);
+    e = cudaGetLastError();
+  } else if (a->out_dtype == OSSM_F32)
     e = launch_out<true, float>(p, lam_tok, st);
   else
     e = precise ? launch_out<true, __nv_bfloat16>(p, lam_tok, st) : launch_out<false, __nv_bfloat16>(p, lam_tok, st);
@@ -810,6 +925,7 @@ int p3_launch_split(const ossm_fwd_args* a, int G, char* ws, cudaStream_t st) {
     off += p3_al(p3_single_bytes(&h));
     if (r != OSSM_OK) break;
     p.ws = header;  // one header: the sticky status lives at the workspace start
+    p.uc = p3_uc_mode(&h);
     r = p3_front(&h, p, streams[g % kStreams]);
     if (r == OSSM_OK) r = p3_back(&h, p, streams[g % kStreams]);
   }
@@ -850,6 +966,8 @@ int p3_launch_seq_split(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
   p1.ws = p0.ws;  // one header: the sticky status lives at the workspace start
   p1.starts_seq = 0;
   p1.carry_in = tot_E;
+  p0.uc = p3_uc_mode(&h0);
+  p1.uc = p3_uc_mode(&h1);
   cudaStream_t side = sd.s[1];
   bool ok = cudaEventRecord(sd.fork, st) == cudaSuccess && cudaStreamWaitEvent(side, sd.fork, 0) == cudaSuccess;
   r = ok ? p3_front(&h0, p0, st) : OSSM_ELAUNCH;
@@ -873,6 +991,7 @@ int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
   p3::Params p;
   int r = p3_params(a, ws, p);
   if (r != OSSM_OK) return r;
+  p.uc = p3_uc_mode(a);
   if ((r = p3_front(a, p, st)) != OSSM_OK) return r;
   return p3_back(a, p, st);
 }
