@@ -8,20 +8,22 @@
 //
 // In that computation every channel (b, h, j) is independent: its gradient
 // and its Lion step use only its own coefficients, momentum and tokens.  The
-// chunk loop therefore moves onto the device, one WARP per channel: the warp
-// walks every chunk of the sequence with the channel's coefficients and Lion
-// momentum in registers (lane k holds c_k and m_k; every lane a broadcast copy
-// of the coefficients).  A chunk is processed in passes of 256 tokens, lane =
-// a run of 8 consecutive tokens:
+// chunk loop therefore moves onto the device, one or two WARPS per channel:
+// they walk every chunk of the sequence with the channel's coefficients and
+// Lion momentum in registers (lane k of the first warp holds c_k and m_k;
+// every lane a broadcast copy of the coefficients).  A chunk is processed in
+// passes of 256 tokens, each warp over 256 / NW of them, lane = a run of
+// 8 / NW consecutive tokens:
 //   1. each lane evaluates its 8 tokens and runs the EMA from zero over them;
 //   2. a warp scan of the runs' (decay product, end state) pairs gives each
-//      run its carry-in (and the pass its carry-out) -- no shared-memory fold
-//      and no CTA barrier;
+//      run its carry-in (and the pass its carry-out); with two warps the
+//      first warp's total reaches the second through shared memory behind a
+//      barrier of the pair;
 //   3. each lane forms its final states, the outputs and its share of the
 //      gated-error gradient;
-// and at the chunk's end a butterfly sum over the lanes (a fixed order) gives
-// the gradient, lanes 0..K-1 take the Lion step and broadcast the new
-// coefficients.  A CTA is 8 warps = 8 adjacent channels of one head: x tiles
+// and at the chunk's end a butterfly sum over the lanes (a fixed order, then
+// the first warp's total plus the second's) gives the gradient, lanes 0..K-1
+// of the first warp take the Lion step and broadcast the new coefficients.  A CTA is 8 warps = 8 adjacent channels of one head: x tiles
 // [257 tokens x 8 channels] are loaded coalesced one pass ahead and
 // transposed through shared memory, and the outputs go back the same way, so
 // the only CTA barrier is one per pass.  The serial chain per channel is one
@@ -34,15 +36,22 @@
 namespace ossm {
 
 namespace lion {
-constexpr int kW = 8;                // warps per CTA = channels per CTA
-constexpr int kNT = kW * 32;
-constexpr int kR = 8;                // tokens per lane per pass
-constexpr int kPass = 32 * kR;       // tokens per pass
-// A channel's tile row holds token t of the pass at (t % 8) * 33 + t / 8
-// (lane-major: lane l reads its r-th token at r * 33 + l, no bank conflicts),
-// the 257th token (the next pass's first) at 8 * 33.
+constexpr int kW = 8;                // channels per CTA
+constexpr int kPass = 256;           // tokens per pass
+// NW warps per channel (1 or 2), each over a part of kPass / NW tokens of
+// every pass, kPass / (32 NW) tokens per lane.  A channel's tile row holds
+// token t = q * (kPass / NW) + l * R + r of the pass (part q, lane l, r-th
+// token of the lane, R = 8 / NW) at (q * R + r) * 33 + l, lane-major so that
+// a warp's read of its r-th tokens hits 32 banks; the 257th token (the next
+// pass's first) at 8 * 33.
 constexpr int kRow = 8 * 33 + 1;
-OSSM_DEV int slot(int t) { return t < kPass ? (t & 7) * 33 + (t >> 3) : 8 * 33; }
+template <int NW>
+OSSM_DEV int slot(int t) {
+  constexpr int R = 8 / NW, HALF = 32 * R;
+  return t < kPass ? ((t / HALF) * R + (t % R)) * 33 + ((t / R) % 32) : 8 * 33;
+}
+// barrier of a channel's two warps (named barrier id, 64 threads)
+OSSM_DEV void pair_sync(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
 }  // namespace lion
 
 struct LionParams {
@@ -107,18 +116,23 @@ OSSM_DEV float eval_one(uint32_t ev, const float2* lut2, int K, const float c[8]
 OSSM_DEV float x_at(const float* p) { return bf16_round(*p); }
 OSSM_DEV float x_at(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-template <typename XT, typename OT>
-__global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
+template <typename XT, typename OT, int NW>
+__global__ void __launch_bounds__(lion::kW * NW * 32) lion_kernel(const LionParams p) {
   using namespace lion;
+  constexpr int kNT = kW * NW * 32, kR = 8 / NW, kHalf = 32 * kR;
   __shared__ float xT[2][kW][kRow];     // x tiles, transposed: [buffer][channel][token]
   __shared__ float oT[2][kW][kRow];     // output tiles, transposed
+  __shared__ float2 tot_s[kW][2];        // each half's (decay product, end state) of the pass
+  __shared__ float gsum_s[kW][8];        // the second half's gradient at a chunk's end
+  __shared__ float cnew_s[kW][8];        // the coefficients after the Lion step
   extern __shared__ float2 lut2[];       // [8 * 256] (LUT evaluation only)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int ci = warp / NW, q = warp % NW;  // channel of the CTA, part of each pass
   const int ngroups = p.HD / kW;
   const int grp = blockIdx.x % ngroups, bh = blockIdx.x / ngroups;
   const int b = bh / p.H, h = bh % p.H;
-  const int j = grp * kW + warp;              // this warp's channel within the head
+  const int j = grp * kW + ci;                // this warp's channel within the head
   const int ch0 = h * p.HD + grp * kW;        // the CTA's first channel within D
   const uint32_t ev = p.flags & OSSM_EVAL_MASK;
   const int Keff = ev == OSSM_EVAL_CLENSHAW_DEG4 ? min(p.K, 4) : p.K;
@@ -134,7 +148,8 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
   const float gamma = 0.98f - 0.06f * (float)h / (float)p.H;
   const float mu = p.mu, oml = 1.f - p.mu;
 
-  // lane k < K holds coefficient k and its Lion momentum; every lane a copy of all
+  // lane k < K holds coefficient k and its Lion momentum (the first half's
+  // warp keeps the Lion state); every lane a copy of all
   const size_t cidx = ((size_t)(b * p.H + h) * p.K + min(lane, p.K - 1)) * p.HD + j;
   float my_c = lane < p.K ? p.coeffs[cidx] : 0.f;
   float my_m = lane < p.K ? p.mom[cidx] : 0.f;
@@ -146,13 +161,13 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
 
   const XT* xb = reinterpret_cast<const XT*>(p.x) + (size_t)b * p.xsb + ch0;
   OT* ob = reinterpret_cast<OT*>(p.out) + (size_t)b * p.osb + ch0;
-  // tile loads: thread r reads token row t0 + r, the CTA's 8 channels; thread
-  // 0 also row t0 + kPass (the next pass's first token)
+  // tile loads: thread r < kPass reads token row t0 + r, the CTA's 8 channels;
+  // thread 0 also row t0 + kPass (the next pass's first token)
   float xr[kW], xe[kW];
   auto load_rows = [&](int t0) {
 #pragma unroll
     for (int c = 0; c < kW; ++c) xr[c] = xe[c] = 0.f;
-    if (t0 + tid < p.S) {
+    if (tid < kPass && t0 + tid < p.S) {
 #pragma unroll
       for (int c = 0; c < kW; ++c) xr[c] = x_at(xb + (size_t)(t0 + tid) * p.xss + c);
     }
@@ -162,14 +177,16 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
     }
   };
   auto store_rows = [&](int bf) {
+    if (tid < kPass) {
 #pragma unroll
-    for (int c = 0; c < kW; ++c) xT[bf][c][slot(tid)] = xr[c];
+      for (int c = 0; c < kW; ++c) xT[bf][c][slot<NW>(tid)] = xr[c];
+    }
     if (tid == 0) {
 #pragma unroll
-      for (int c = 0; c < kW; ++c) xT[bf][c][slot(kPass)] = xe[c];
+      for (int c = 0; c < kW; ++c) xT[bf][c][slot<NW>(kPass)] = xe[c];
     }
   };
-  static_assert(kNT == kPass, "one thread per tile row");
+  static_assert(kNT >= kPass, "one thread per tile row");
 
   int buf = 0;
   load_rows(0);
@@ -180,7 +197,7 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
   for (int cs = 0; cs < p.S; cs += p.chunk) {
     const int ce = min(cs + p.chunk, p.S);
     const int Lc = ce - cs;
-    if (p.trace && lane < p.K)  // the chunk's starting coefficients, for the backward
+    if (p.trace && q == 0 && lane < p.K)  // the chunk's starting coefficients, for the backward
       p.trace[(size_t)(cs / p.chunk) * ((size_t)p.B * p.H * p.K * p.HD) + cidx] = my_c;
     float ceff[8];
 #pragma unroll
@@ -194,14 +211,14 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
       // the next pass's rows (next chunk's first pass at a chunk's end) in flight
       const int nps = ps + kPass < ce ? ps + kPass : ce;
       load_rows(nps);
-      const int tb = ps + lane * kR;
-      // -- 1: the lane's 8 tokens from state 0; xn of 9 tokens (the 9th is the
+      const int tb = ps + q * kHalf + lane * kR;
+      // -- 1: the lane's 4 tokens from state 0; xn of 5 tokens (the 5th is the
       //       next run's first, for the prediction error of the last)
       float sl[kR], xn[kR + 1];
       float s = 0.f, Arun = 1.f;
 #pragma unroll
       for (int r = 0; r <= kR; ++r) {
-        const float xv = xT[buf][warp][r < kR ? r * 33 + lane : slot(lane * kR + kR)];
+        const float xv = xT[buf][ci][r < kR ? (q * kR + r) * 33 + lane : slot<NW>(q * kHalf + lane * kR + kR)];
         float xa, sg;
         xn[r] = softsign<true>(xv, false, xa, sg);
         if (r < kR) {
@@ -215,7 +232,7 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
           }
           sl[r] = s;
           if (p.tanh_out && valid)
-            p.tanh_out[(size_t)b * p.osb + (size_t)(tb + r) * p.oss + ch0 + warp] = u;
+            p.tanh_out[(size_t)b * p.osb + (size_t)(tb + r) * p.oss + ch0 + ci] = u;
         }
       }
       // -- 2: carries of the runs: inclusive scan of (A, B), then shift by one
@@ -228,9 +245,20 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
           A *= Ao;
         }
       }
+      // the two halves' totals through shared memory: half 1 enters from the
+      // state after half 0; both fold the pass's carry-out in the same order
+      float cq = carry;
+      if (NW == 2) {
+        if (lane == 31) tot_s[ci][q] = make_float2(A, Bs);
+        pair_sync(1 + ci);
+        const float2 t0v = tot_s[ci][0], t1v = tot_s[ci][1];
+        if (q == 1) cq = fmaf(t0v.x, carry, t0v.y);
+        carry = fmaf(t1v.x, fmaf(t0v.x, carry, t0v.y), t1v.y);
+      } else {
+        carry = fmaf(__shfl_sync(0xffffffffu, A, 31), carry, __shfl_sync(0xffffffffu, Bs, 31));
+      }
       const float Ae = __shfl_up_sync(0xffffffffu, A, 1), Be = __shfl_up_sync(0xffffffffu, Bs, 1);
-      const float cin = lane == 0 ? carry : fmaf(Ae, carry, Be);
-      carry = fmaf(__shfl_sync(0xffffffffu, A, 31), carry, __shfl_sync(0xffffffffu, Bs, 31));
+      const float cin = lane == 0 ? cq : fmaf(Ae, cq, Be);
       // -- 3: final states, outputs, the gated-error gradient (:2141-2169)
       float Acum = 1.f;
 #pragma unroll
@@ -239,7 +267,7 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
         if (t < ce) {
           Acum *= mu;
           const float sf = clamp1(fmaf(Acum, cin, sl[r]));
-          oT[buf][warp][r * 33 + lane] = sizeof(OT) == 4 ? bf16_round(sf) : sf;
+          oT[buf][ci][(q * kR + r) * 33 + lane] = sizeof(OT) == 4 ? bf16_round(sf) : sf;
           // e = xn_{t+1} - s_t, weight sigmoid(3|e|), Chebyshev basis of xn_t
           const float e = t + 1 < ce ? xn[r + 1] - sf : 0.f;
           const float w = __frcp_rn(1.0f + __expf(-3.0f * fabsf(e)));
@@ -264,8 +292,8 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
         OT* op = ob + (size_t)(ps + tid) * p.oss;
 #pragma unroll
         for (int c = 0; c < kW; c += 4)
-          st4(op + c, make_float4(oT[buf][c][slot(tid)], oT[buf][c + 1][slot(tid)], oT[buf][c + 2][slot(tid)],
-                                  oT[buf][c + 3][slot(tid)]));
+          st4(op + c, make_float4(oT[buf][c][slot<NW>(tid)], oT[buf][c + 1][slot<NW>(tid)], oT[buf][c + 2][slot<NW>(tid)],
+                                  oT[buf][c + 3][slot<NW>(tid)]));
       }
       buf ^= 1;
     }
@@ -279,7 +307,14 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
 #pragma unroll
     for (int k = 1; k < 8; ++k)
       if (lane == k) gk = g[k];
-    if (lane < p.K) {
+    // half 0's gradient + half 1's (a fixed order), then the Lion step in half
+    // 0's lanes, its result to both halves
+    if (NW == 2) {
+      if (q == 1 && lane < 8) gsum_s[ci][lane] = gk;
+      pair_sync(1 + ci);
+      if (q == 0 && lane < 8) gk += gsum_s[ci][lane];
+    }
+    if (q == 0 && lane < p.K) {
       // the reference divides by Lc - 1 (NaN for a 1-token chunk); a 1-token
       // chunk has no prediction pair and contributes no gradient.
       const float gr = Lc > 1 ? gk * (1.0f / (float)(Lc - 1)) : 0.f;
@@ -288,15 +323,22 @@ __global__ void __launch_bounds__(lion::kNT) lion_kernel(const LionParams p) {
       my_m = p.beta2 * my_m + (1.0f - p.beta2) * gr;
       my_c = decay * my_c + lr * p.ss[lane] * sgn;
     }
+    if (NW == 2) {
+      if (q == 0 && lane < 8) cnew_s[ci][lane] = my_c;
+      pair_sync(1 + ci);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) cf[k] = __shfl_sync(0xffffffffu, my_c, k);
+      for (int k = 0; k < 8; ++k) cf[k] = cnew_s[ci][k];
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) cf[k] = __shfl_sync(0xffffffffu, my_c, k);
+    }
   }
 
-  if (lane < p.K) {
+  if (q == 0 && lane < p.K) {
     p.coeffs[cidx] = my_c;
     p.mom[cidx] = my_m;
   }
-  if (p.fin && lane == 0) p.fin[(size_t)b * p.D + h * p.HD + j] = carry;
+  if (p.fin && q == 0 && lane == 0) p.fin[(size_t)b * p.D + h * p.HD + j] = carry;
 }
 
 }  // namespace ossm
@@ -306,13 +348,27 @@ using namespace ossm;
 namespace {
 bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 
+// Two warps per channel while the grid (8 channels a CTA) leaves SMs free,
+// else one: at 128 registers a thread the SM holds one 16-warp CTA or two
+// 8-warp ones.  Measured at B = 2 x S = 65536 (128 CTAs): 1.50 against
+// 1.67 ms (LUT); at B = 8 x S = 16384 (512 CTAs) one warp per channel is
+// faster (0.90 against 1.22 ms).
+template <typename XT, typename OT, int NW>
+cudaError_t launch_lion_nw(const LionParams& p, int grid, cudaStream_t st) {
+  const size_t dyn = (p.flags & OSSM_EVAL_MASK) == OSSM_EVAL_LUT ? 8 * 256 * sizeof(float2) : 0;
+  cudaError_t e =
+      cudaFuncSetAttribute(lion_kernel<XT, OT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+  if (e != cudaSuccess) return e;
+  lion_kernel<XT, OT, NW><<<grid, lion::kW * NW * 32, dyn, st>>>(p);
+  return cudaGetLastError();
+}
 template <typename XT, typename OT>
 cudaError_t launch_lion(const LionParams& p, int grid, cudaStream_t st) {
-  const size_t dyn = (p.flags & OSSM_EVAL_MASK) == OSSM_EVAL_LUT ? 8 * 256 * sizeof(float2) : 0;
-  cudaError_t e = cudaFuncSetAttribute(lion_kernel<XT, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+  int dev = 0, nsm = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  lion_kernel<XT, OT><<<grid, lion::kNT, dyn, st>>>(p);
-  return cudaGetLastError();
+  return grid <= nsm ? launch_lion_nw<XT, OT, 2>(p, grid, st) : launch_lion_nw<XT, OT, 1>(p, grid, st);
 }
 }  // namespace
 
