@@ -94,7 +94,8 @@ def test_golden_fast_path_routing():
 
 @pytest.mark.parametrize("B,S,D,H,K,chunk", [(2, 1024, 128, 8, 8, 256), (1, 2048, 512, 8, 8, 256),
                                              (3, 1000, 64, 4, 4, 300), (1, 257, 64, 8, 8, 256),
-                                             (2, 700, 256, 8, 6, 2048)])
+                                             (2, 700, 256, 8, 6, 2048),
+                                             (3, 600, 512, 8, 8, 256)])  # 192 CTAs: one warp per channel
 def test_oracle_shapes(B, S, D, H, K, chunk):
     x = det_normal((B, S, D), 200 + S)
     c = spectral_coeffs(B, H, K, D // H, 201, scale=0.5)
