@@ -20,12 +20,12 @@
 //                              kind::tf32 product instead);
 //     warps 2-5 read the accumulator back (tcgen05.ld), scale by 2/N and
 //     stage the tile in shared memory, from where TMA stores gs (t < L-1)
-//     and the same warps form the reverse scan's record of each 64-token
+//     and the same warps form the reverse scan's record of each 32-token
 //     block (the adjoint at its first token from a zero carry, and the decay
 //     product applied to the carry);
 //   ttt_grad_kernel  CTA per (sequence, 64 channels, 8 blocks), warp per
-//     32-token block, a channel pair per lane: folds the later blocks' records into its incoming
-//     adjoint (no carry pass), runs the reverse adjoint over its tokens and
+//     32-token block, a channel pair per lane: folds the later blocks'
+//     records into its incoming adjoint (no carry pass), runs the reverse adjoint over its tokens and
 //     sums the coefficient gradient; the CTA's blocks are summed in shared
 //     memory, and the last CTA of each (sequence, channel group) sums the
 //     CTAs in order and applies the spectral scale and Adam.
