@@ -414,6 +414,8 @@ def run_ours(args):
                          "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                          "peak_kind": peak_kind, "bytes_per_step": scan_bytes,
                          "avg_step_ms": scan_avg},
+            # the XU (MUFU) pipe: one reciprocal and one tanh per element in each of the two passes
+            "sfu": sfu_record(4 * elem, scan_avg, clocks, dev),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": elem * 2 + B * D * 4,
                     "d2h_bytes_per_step": elem * 2 + B * D * 4},
             "clocks": clocks,
@@ -519,6 +521,20 @@ def seqpar_record(args, world, rank, dev, stream, barrier, max_over_ranks):
             "hbm_gbs_per_gpu": gbs, "hbm_frac_per_gpu": gbs / peak, "peak_kind": kind,
             "parity_ok": bool(err <= 2 ** -7 and ferr < 1e-4), "max_abs_err_vs_unsharded": err,
             "final_state_relerr_vs_unsharded": ferr, "device_status": O.workspace_status()}
+
+
+def sfu_record(ops, step_ms, clocks, dev):
+    """MUFU operations per step against the XU pipe's 16 operations per SM
+    per clock at the median SM clock sampled under load (a tanh.approx.f32
+    throughput probe on this pool's B200s measured 4.61 T operations/s,
+    148 x 16 x 1.95 GHz)."""
+    import torch
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+    mhz = (clocks or {}).get("sm_mhz") or (clocks or {}).get("sm_max_mhz") or 1965.0
+    peak = nsm * 16 * mhz * 1e6
+    achieved = ops / (step_ms / 1e3)
+    return {"ops_per_step": ops, "achieved_tops": achieved / 1e12, "peak_tops": peak / 1e12,
+            "frac": achieved / peak, "peak_kind": "16 per SM per clock at the sampled SM clock"}
 
 
 def tensor_peak():
