@@ -266,34 +266,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       bulk_commit();
     }
     if (ok) {
-      // thread e: columns e and e + 128, one reverse pass over the tile's rows
-      // (R_t = g_t + a_{t+1} R_{t+1}, the reverse adjoint from a zero carry),
-      // a record at each 64-token block's first token
+      // thread e: columns e and e + 128 of each of the tile's 32-token blocks,
+      // the 8 reverse chains (R_t = g_t + a_{t+1} R_{t+1}, the reverse adjoint
+      // from a zero carry at the block's end) interleaved row by row, and a
+      // record at each block's first token
+      constexpr int kNB = kBM / kBlk;
       const int e = threadIdx.x - 64;
       const int c0 = e, c1 = e + 128, hh0 = c0 / p.HD, hh1 = c1 / p.HD;
       auto gat = [&](int rr, int col) {
         return *reinterpret_cast<const float*>(smem + (col >> 5) * kBoxBytes + rr * 128 +
                                                (((((col & 31) >> 2) ^ (rr & 7))) << 4) + (col & 3) * 4);
       };
-      float R0 = 0.f, R1 = 0.f, A0 = 1.f, A1 = 1.f;
-      const int top = min(kBM, p.L - m0) - 1;
-#pragma unroll 8
-      for (int rr = top; rr >= 0; --rr) {
-        const float a0 = dsm[rr * nh + hh0], a1 = dsm[rr * nh + hh1];
-        R0 = fmaf(a0, R0, gat(rr, c0));
-        R1 = fmaf(a1, R1, gat(rr, c1));
-        A0 *= a0;
-        A1 *= a1;
-        if ((rr & (kBlk - 1)) == 0) {
-          const int blk = (m0 + rr) / kBlk;
-          float* rec = p.Rrec + ((size_t)b * p.nblk + blk) * p.D + n0;
-          rec[c0] = R0;
-          rec[c1] = R1;
-          if (c0 % p.HD == 0) p.Arec[((size_t)b * p.nblk + blk) * p.H + h0 + hh0] = A0;
-          if (c1 % p.HD == 0) p.Arec[((size_t)b * p.nblk + blk) * p.H + h0 + hh1] = A1;
-          R0 = R1 = 0.f;
-          A0 = A1 = 1.f;
+      const int nrows = min(kBM, p.L - m0);  // rows of the tile inside the chunk
+      float R0[kNB], R1[kNB], A0[kNB], A1[kNB];
+#pragma unroll
+      for (int qb = 0; qb < kNB; ++qb) {
+        R0[qb] = R1[qb] = 0.f;
+        A0[qb] = A1[qb] = 1.f;
+      }
+#pragma unroll 4
+      for (int i = kBlk - 1; i >= 0; --i) {
+#pragma unroll
+        for (int qb = 0; qb < kNB; ++qb) {
+          const int rr = qb * kBlk + i;
+          if (rr < nrows) {
+            const float a0 = dsm[rr * nh + hh0], a1 = dsm[rr * nh + hh1];
+            R0[qb] = fmaf(a0, R0[qb], gat(rr, c0));
+            R1[qb] = fmaf(a1, R1[qb], gat(rr, c1));
+            A0[qb] *= a0;
+            A1[qb] *= a1;
+          }
         }
+      }
+#pragma unroll
+      for (int qb = 0; qb < kNB; ++qb) {
+        if (qb * kBlk >= nrows) break;
+        const int blk = m0 / kBlk + qb;
+        float* rec = p.Rrec + ((size_t)b * p.nblk + blk) * p.D + n0;
+        rec[c0] = R0[qb];
+        rec[c1] = R1[qb];
+        if (c0 % p.HD == 0) p.Arec[((size_t)b * p.nblk + blk) * p.H + h0 + hh0] = A0[qb];
+        if (c1 % p.HD == 0) p.Arec[((size_t)b * p.nblk + blk) * p.H + h0 + hh1] = A1[qb];
       }
     }
     if (ok && threadIdx.x == 64) bulk_wait_read0();  // the store has read the tile before the CTA exits
