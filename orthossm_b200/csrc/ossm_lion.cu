@@ -220,12 +220,14 @@ __global__ void __launch_bounds__(lion::kW * NW * 32) lion_kernel(const LionPara
       for (int r = 0; r <= kR; ++r) {
         const float xv = xT[buf][ci][r < kR ? (q * kR + r) * 33 + lane : slot<NW>(q * kHalf + lane * kR + kR)];
         float xa, sg;
-        xn[r] = softsign<true>(xv, false, xa, sg);
+        xn[r] = softsign<false>(xv, false, xa, sg);  // approximate reciprocal, as the reference's division
         if (r < kR) {
           const bool valid = tb + r < ce;
           const float y = eval_one(ev, lut2, p.K, ceff, xn[r], xa, sg) * gamma;
           const float yc = fminf(fmaxf(y, -4.f), 4.f);
-          const float u = (xv != xv || !valid) ? 0.f : tanhf(yc);
+          // the reference's stable tanh, (e^{2y} - 1) / (e^{2y} + 1) on the clamped y (:2083-2086)
+          const float e2y = __expf(2.f * yc);
+          const float u = (xv != xv || !valid) ? 0.f : __fdividef(e2y - 1.f, e2y + 1.f);
           if (valid) {
             s = fmaf(mu, s, oml * u);
             Arun *= mu;
