@@ -105,3 +105,51 @@ def test_run_single_token_chunks_and_inputs_untouched():
         else:
             assert relerr(r["out"].cpu().numpy(), f["out"].cpu().numpy()) < 1e-3
     assert np.array_equal(cT.cpu().numpy(), c) and not mT.abs().sum().item()
+
+
+def test_run_c_abi_rejects_unsupported_shapes_and_small_workspaces():
+    """Through the C ABI: H*head_dim not a multiple of 256 is rejected (size
+    query 0, OSSM_EINVAL), a workspace one byte short gives OSSM_EWORKSPACE,
+    and neither launches anything (the coefficients are unchanged)."""
+    from orthossm_b200 import _lib as L
+    lib = L.lib()
+    st = torch.cuda.current_stream().cuda_stream
+
+    def case(H, hd, seed):
+        B, S = 1, 256
+        x, c, Wp, _, _, _, lam = _inputs(B, S, H, hd, seed, False, False)
+        t = dict(x=T(x, torch.bfloat16), c=T(c), w=T(Wp), lam=T(lam), out=torch.empty(B, S, H * hd, device="cuda"))
+        t["m"], t["v"] = torch.zeros_like(t["c"]), torch.zeros_like(t["c"])
+        a = L.TttRunArgs(B=B, S=S, H=H, head_dim=hd, degree=8, chunk=128, x=t["x"].data_ptr(), x_dtype=L.OSSM_BF16,
+                         x_stride_b=t["x"].stride(0), x_stride_s=t["x"].stride(1), coeffs=t["c"].data_ptr(),
+                         m=t["m"].data_ptr(), v=t["v"].data_ptr(), lam_h=t["lam"].data_ptr(), momentum=0.9,
+                         w_pred=t["w"].data_ptr(), out=t["out"].data_ptr(), lr=1e-3, beta1=0.9, beta2=0.999,
+                         eps=1e-8, spectral_pow=2.0, step0=0, forget=1, flags=0)
+        return a, t, c
+
+    a, t, c = case(8, 16, 2400)  # D = 128
+    assert lib.ossm_ttt_run_workspace_bytes(L.C.byref(a)) == 0
+    ws = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    assert lib.ossm_ttt_wpred_run(L.C.byref(a), ws.data_ptr(), ws.numel(), st) == L.OSSM_EINVAL
+    a5, t5, c5 = case(8, 64, 2401)  # D = 512: taken, but one byte short of the workspace is refused
+    need = lib.ossm_ttt_run_workspace_bytes(L.C.byref(a5))
+    assert need > 0
+    ws5 = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    assert lib.ossm_ttt_wpred_run(L.C.byref(a5), ws5.data_ptr(), need - 1, st) == L.OSSM_EWORKSPACE
+    torch.cuda.synchronize()
+    assert np.array_equal(t["c"].cpu().numpy(), c) and np.array_equal(t5["c"].cpu().numpy(), c5)
+
+
+def test_unsupported_width_takes_the_library_gemm_loop():
+    """H*head_dim = 128 (not a multiple of 256): ttt_wpred_adam runs the
+    chunk loop with the W_pred products on cuBLAS and still matches the oracle."""
+    B, S, H, hd, chunk = 2, 256, 8, 16, 128
+    x, c, Wp, W, b, ini, lam = _inputs(B, S, H, hd, 2500, False, True)
+    nat = _run(x, c, Wp, None, None, ini, lam, chunk, "tf32")
+    z = np.zeros_like(c)
+    ref = R.ttt_wpred_adam(x.astype(np.float64), c.astype(np.float64), z, z, 0, Wp.astype(np.float64),
+                           lam.astype(np.float64), gate=None, init=ini.astype(np.float64), chunk=chunk)
+    assert nat["step"] == ref["step"] == 2
+    assert relerr(nat["out"], ref["out"]) < 5e-3
+    moved = np.abs(nat["coeffs"] - ref["c"]) > 1e-5
+    assert moved.mean() < 0.01, moved.mean()
