@@ -35,6 +35,8 @@
 // one workspace: 3 launches per chunk after the forward's.
 #include <cudaTypedefs.h>
 
+#include <type_traits>
+
 #include "orthossm_b200.h"
 #include "ossm_eval.cuh"
 
@@ -505,67 +507,77 @@ __global__ void __launch_bounds__(256, 2) ttt_grad_kernel(const RParams p) {
   // tokens in batches of 8; the next batch's x is loaded once this batch's
   // xn is formed, its gs once this batch's adjoint is done, so both are in
   // flight while the other half of the work runs
-  float2 gv[8], xv[8];
-  auto load_g = [&](int tb) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int t = tb - i;
-      gv[i] = (t >= t0 && t < p.L - 1) ? __ldcg(reinterpret_cast<const float2*>(gp + (size_t)t * p.D))
-                                       : make_float2(0.f, 0.f);
+  // A full block (all kBlk tokens inside the chunk, the common case) runs
+  // without the per-token range checks.
+  auto walk = [&](auto full_tag) {
+    constexpr bool FULL = decltype(full_tag)::value;
+    const int tlast = FULL ? t0 + kBlk - 1 : t1 - 1;
+    float2 gv[8], xv[8];
+    auto load_g = [&](int tb) {
+  #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int t = tb - i;
+        gv[i] = ((FULL || t >= t0) && t < p.L - 1) ? __ldcg(reinterpret_cast<const float2*>(gp + (size_t)t * p.D))
+                                         : make_float2(0.f, 0.f);
+      }
+    };
+    auto load_x = [&](int tb) {
+  #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int t = tb - i;
+        if (!FULL && t < t0) {
+          xv[i] = make_float2(0.f, 0.f);
+        } else if (p.x_bf16) {
+          const uint32_t r = *reinterpret_cast<const uint32_t*>(xp + t * xrow);
+          xv[i] = make_float2(__uint_as_float(r << 16), __uint_as_float(r & 0xffff0000u));
+        } else {
+          xv[i] = *reinterpret_cast<const float2*>(xp + t * xrow);
+        }
+      }
+    };
+    load_x(tlast);
+    load_g(tlast);
+    for (int tb = tlast; tb >= t0; tb -= 8) {
+      const bool more = tb - 8 >= t0;
+      // per token, independent of the adjoint: xn and the factor
+      // w = (1 - a_t) (1 - u^2) gamma [|z| < 4] (0 for NaN x, where u = 0)
+      float2 xn[8], w[8];
+  #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        xn[i] = softsign2(xv[i]);
+        float2 z = mc[7];
+  #pragma unroll
+        for (int q = 6; q >= 0; --q) z = fma2(z, xn[i], mc[q]);
+        const float f = (FULL || tb - i >= t0) ? (1.f - dec(tb - i)) * gamma : 0.f;
+        w[i] = make_float2((xv[i].x == xv[i].x && fabsf(z.x) < 4.f) ? f * sech2(z.x) : 0.f,
+                           (xv[i].y == xv[i].y && fabsf(z.y) < 4.f) ? f * sech2(z.y) : 0.f);
+      }
+      if (more) load_x(tb - 8);
+      // the serial adjoint, then dy T_k into the gradient
+  #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float an = (FULL || tb - i >= t0) ? dec(tb - i + 1) : 1.f;
+        adj = fma2(make_float2(an, an), adj, gv[i]);
+        const float2 dy = mul2(w[i], adj);
+        const float2 x2 = fma2(xn[i], make_float2(2.f, 2.f), make_float2(0.f, 0.f));
+        float2 ta = make_float2(1.f, 1.f), tb2 = xn[i];
+        acc[0] = fma2(dy, ta, acc[0]);
+        acc[1] = fma2(dy, tb2, acc[1]);
+  #pragma unroll
+        for (int k = 2; k < 8; ++k) {
+          const float2 tc = sub2(mul2(x2, tb2), ta);
+          acc[k] = fma2(dy, tc, acc[k]);
+          ta = tb2;
+          tb2 = tc;
+        }
+      }
+      if (more) load_g(tb - 8);
     }
   };
-  auto load_x = [&](int tb) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int t = tb - i;
-      if (t < t0) {
-        xv[i] = make_float2(0.f, 0.f);
-      } else if (p.x_bf16) {
-        const uint32_t r = *reinterpret_cast<const uint32_t*>(xp + t * xrow);
-        xv[i] = make_float2(__uint_as_float(r << 16), __uint_as_float(r & 0xffff0000u));
-      } else {
-        xv[i] = *reinterpret_cast<const float2*>(xp + t * xrow);
-      }
-    }
-  };
-  load_x(t1 - 1);
-  load_g(t1 - 1);
-  for (int tb = t1 - 1; tb >= t0; tb -= 8) {
-    const bool more = tb - 8 >= t0;
-    // per token, independent of the adjoint: xn and the factor
-    // w = (1 - a_t) (1 - u^2) gamma [|z| < 4] (0 for NaN x, where u = 0)
-    float2 xn[8], w[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      xn[i] = softsign2(xv[i]);
-      float2 z = mc[7];
-#pragma unroll
-      for (int q = 6; q >= 0; --q) z = fma2(z, xn[i], mc[q]);
-      const float f = (tb - i >= t0) ? (1.f - dec(tb - i)) * gamma : 0.f;
-      w[i] = make_float2((xv[i].x == xv[i].x && fabsf(z.x) < 4.f) ? f * sech2(z.x) : 0.f,
-                         (xv[i].y == xv[i].y && fabsf(z.y) < 4.f) ? f * sech2(z.y) : 0.f);
-    }
-    if (more) load_x(tb - 8);
-    // the serial adjoint, then dy T_k into the gradient
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float an = tb - i >= t0 ? dec(tb - i + 1) : 1.f;
-      adj = fma2(make_float2(an, an), adj, gv[i]);
-      const float2 dy = mul2(w[i], adj);
-      const float2 x2 = fma2(xn[i], make_float2(2.f, 2.f), make_float2(0.f, 0.f));
-      float2 ta = make_float2(1.f, 1.f), tb2 = xn[i];
-      acc[0] = fma2(dy, ta, acc[0]);
-      acc[1] = fma2(dy, tb2, acc[1]);
-#pragma unroll
-      for (int k = 2; k < 8; ++k) {
-        const float2 tc = sub2(mul2(x2, tb2), ta);
-        acc[k] = fma2(dy, tc, acc[k]);
-        ta = tb2;
-        tb2 = tc;
-      }
-    }
-    if (more) load_g(tb - 8);
-  }
+  if (t1 - t0 == kBlk)
+    walk(std::true_type{});
+  else
+    walk(std::false_type{});
 
   // the CTA's 8 blocks in block order, then one partial per CTA
 #pragma unroll
