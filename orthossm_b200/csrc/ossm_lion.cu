@@ -125,7 +125,11 @@ __global__ void __launch_bounds__(lion::kW * NW * 32) lion_kernel(const LionPara
   __shared__ float2 tot_s[kW][2];        // each half's (decay product, end state) of the pass
   __shared__ float gsum_s[kW][8];        // the second half's gradient at a chunk's end
   __shared__ float cnew_s[kW][8];        // the coefficients after the Lion step
-  extern __shared__ float2 lut2[];       // [8 * 256] (LUT evaluation only)
+  // LUT evaluation only: the table as (T_k[i], T_k[i+1]) pairs [8][256], then
+  // per channel the coefficient-weighted sums of its even and odd rows in the
+  // same pair form [kW][2][256], rebuilt at every chunk's start
+  extern __shared__ float2 lut2[];
+  float2* comb = lut2 + 8 * 256;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int ci = warp / NW, q = warp % NW;  // channel of the CTA, part of each pass
@@ -202,6 +206,28 @@ __global__ void __launch_bounds__(lion::kW * NW * 32) lion_kernel(const LionPara
     float ceff[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) ceff[k] = k < Keff ? cf[k] : 0.f;
+    if (ev == OSSM_EVAL_LUT) {  // y(xa) = E(xa) + sgn O(xa): the interpolation is linear in the rows
+      float2* ce2 = comb + ci * 2 * 256;
+      for (int i = q * 32 + lane; i < 256; i += NW * 32) {
+        float2 e = make_float2(0.f, 0.f), o = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (k < p.K) {
+            const float2 tt = lut2[k * 256 + i];
+            if (k & 1)
+              o = make_float2(fmaf(ceff[k], tt.x, o.x), fmaf(ceff[k], tt.y, o.y));
+            else
+              e = make_float2(fmaf(ceff[k], tt.x, e.x), fmaf(ceff[k], tt.y, e.y));
+          }
+        }
+        ce2[i] = e;
+        ce2[256 + i] = o;
+      }
+      if (NW == 2)
+        pair_sync(1 + ci);
+      else
+        __syncwarp();
+    }
     float g[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) g[k] = 0.f;
@@ -223,7 +249,17 @@ __global__ void __launch_bounds__(lion::kW * NW * 32) lion_kernel(const LionPara
         xn[r] = softsign<false>(xv, false, xa, sg);  // approximate reciprocal, as the reference's division
         if (r < kR) {
           const bool valid = tb + r < ce;
-          const float y = eval_one(ev, lut2, p.K, ceff, xn[r], xa, sg) * gamma;
+          float y;
+          if (ev == OSSM_EVAL_LUT) {  // sdpc_kernel.py:2030-2069, rows combined per chunk
+            const float fidx = xa * 255.0f;
+            int i0 = max((int)fidx, 0);
+            if (i0 >= 255) i0 = 254;
+            const float fr = fminf(fmaxf(fidx - (float)i0, 0.f), 1.f);
+            const float2 e = comb[ci * 2 * 256 + i0], o = comb[ci * 2 * 256 + 256 + i0];
+            y = fmaf(sg, fmaf(fr, o.y - o.x, o.x), fmaf(fr, e.y - e.x, e.x)) * gamma;
+          } else {
+            y = eval_one(ev, lut2, p.K, ceff, xn[r], xa, sg) * gamma;
+          }
           const float yc = fminf(fmaxf(y, -4.f), 4.f);
           // the reference's stable tanh, (e^{2y} - 1) / (e^{2y} + 1) on the clamped y (:2083-2086)
           const float e2y = __expf(2.f * yc);
@@ -357,7 +393,7 @@ bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 // faster (0.90 against 1.22 ms).
 template <typename XT, typename OT, int NW>
 cudaError_t launch_lion_nw(const LionParams& p, int grid, cudaStream_t st) {
-  const size_t dyn = (p.flags & OSSM_EVAL_MASK) == OSSM_EVAL_LUT ? 8 * 256 * sizeof(float2) : 0;
+  const size_t dyn = (p.flags & OSSM_EVAL_MASK) == OSSM_EVAL_LUT ? (8 + 2 * lion::kW) * 256 * sizeof(float2) : 0;
   cudaError_t e =
       cudaFuncSetAttribute(lion_kernel<XT, OT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
   if (e != cudaSuccess) return e;
