@@ -14,7 +14,10 @@
 // every lane a broadcast copy of the coefficients).  A chunk is processed in
 // passes of 256 tokens, each warp over 256 / NW of them, lane = a run of
 // 8 / NW consecutive tokens:
-//   1. each lane evaluates its 8 tokens and runs the EMA from zero over them;
+//   1. each lane evaluates its 8 / NW tokens and runs the EMA from zero over
+//      them (LUT evaluation reads two per-channel tables rebuilt at each
+//      chunk's start: the coefficient-weighted sums of the even and of the
+//      odd rows, as the interpolation is linear in the rows);
 //   2. a warp scan of the runs' (decay product, end state) pairs gives each
 //      run its carry-in (and the pass its carry-out); with two warps the
 //      first warp's total reaches the second through shared memory behind a
@@ -23,7 +26,8 @@
 //      gated-error gradient;
 // and at the chunk's end a butterfly sum over the lanes (a fixed order, then
 // the first warp's total plus the second's) gives the gradient, lanes 0..K-1
-// of the first warp take the Lion step and broadcast the new coefficients.  A CTA is 8 warps = 8 adjacent channels of one head: x tiles
+// of the first warp take the Lion step and broadcast the new coefficients.
+// A CTA holds 8 adjacent channels of one head (8 NW warps): x tiles
 // [257 tokens x 8 channels] are loaded coalesced one pass ahead and
 // transposed through shared memory, and the outputs go back the same way, so
 // the only CTA barrier is one per pass.  The serial chain per channel is one
