@@ -501,7 +501,29 @@ def seqpar_record(args, world, rank, dev, stream, barrier, max_over_ranks):
     else:
         fn = lambda: O.cheby_ema_forward(xs, c, lambda_per_head=lam, out=out)  # noqa: E731
     steps = max(3, min(args.steps, 20))
-    ms = _timed(fn, steps, args.warmup, stream, barrier, max_over_ranks)
+    ms_direct = _timed(fn, steps, args.warmup, stream, barrier, max_over_ranks)
+    # the same step as one CUDA graph (its all-gather included): at 8 ranks a
+    # step is ~0.1 ms of GPU work, near the host's own cost of enqueuing it
+    ms = ms_direct
+    graph = torch.cuda.CUDAGraph()
+    captured = 1.0
+    try:
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(graph, stream=stream):
+                fn()
+        torch.cuda.synchronize()
+    except Exception:
+        captured = 0.0
+    barrier()
+    if world > 1:  # every rank replays, or none
+        flag = torch.tensor([captured], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        captured = float(flag.item())
+    if captured:
+        ms = _timed(graph.replay, steps, args.warmup, stream, barrier, max_over_ranks)
+    del graph
+    torch.cuda.synchronize()
+    barrier()
     with torch.cuda.stream(stream):
         _, fin = fn()
         full, fin_full = O.cheby_ema_forward(x, c, lambda_per_head=lam)
@@ -516,6 +538,8 @@ def seqpar_record(args, world, rank, dev, stream, barrier, max_over_ranks):
     return {"workload": "cfg3: one sequence of 1,048,576 tokens, D=512, degree 8, bf16 in/out, per-head decays, "
                         "no gate, sequence-sharded over the ranks", "n_gpus": world, "scaling": "strong",
             "tokens_per_s": S_all / (step_ms / 1e3), "ms_per_sequence": step_ms, "steps": steps,
+            "timing": "CUDA-graph replay" if captured else "plain calls",
+            "ms_per_sequence_direct": ms_direct / steps,
             "parallelism": ("sequence-sharded x%d: shard aggregates, one NCCL all-gather of the packed shard "
                             "totals, device fold, shard outputs" % world) if world > 1 else "one GPU, unsharded",
             "hbm_gbs_per_gpu": gbs, "hbm_frac_per_gpu": gbs / peak, "peak_kind": kind,
