@@ -31,6 +31,7 @@
 // NaN inputs are handled off the hot path: the fast evaluation lets them
 // surface as NaN, each warp checks its chunk once and recomputes it with the
 // reference's semantics (u = 0 there).
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -124,6 +125,7 @@ struct Params {
   const float* lam_in;  // caller's per-token decay [B,S,H] or NULL
   float* lam_ws;        // per-token decays written by the gate [B,S,H] (workspace)
   float4* cmono;        // [B*8][4][32]: each lane's gamma-folded, 4^-k-scaled monomial coefficients
+  uint32_t* noclamp;    // [B*8]: 1 where the head's polynomial stays inside the clamp (clamp_free_bound)
   uint4* wfrag;         // [8][4][32]: each lane's mma B fragments of the gate weights, bf16 hi + lo
   const float* init;
   float* fin;
@@ -147,7 +149,53 @@ struct Params {
   // 1: the aggregate pass parks u (fp32) in the fp32 output buffer and the
   // output pass reads it back instead of evaluating again
   int uc;
+  // bf16 outputs: the aggregate pass parks u as fp16 pairs in this L2-resident
+  // ring slot, [B][nchunks][8 heads][32 tokens][32 lanes] words, and the
+  // output pass reads it back (or NULL: the output pass evaluates again)
+  uint32_t* park;
+  // With park, the aggregate pass also forms the carries (no carry pass):
+  // spans of kSpanC chunks, folded by the span's last CTA to finish (an
+  // atomic ticket per span), then the spans folded by the sequence's last.
+  int nsp;            // spans per sequence
+  uint32_t* tk_span;  // [B][nsp] tickets (zero between launches)
+  uint32_t* tk_seq;   // [B] tickets
+  float* spA;         // [B*8][nsp] span decay products
+  float* spE;         // [B*8][nsp][64] span end states from zero
+  float* spX;         // [B*8][nsp][64] state entering each span
+  uint32_t* zero_ptr;  // p3_prep_kernel clears these words first (or NULL)
+  int zero_n;
 };
+constexpr int kSpanC = 16;  // chunks per span of the in-pass carry
+
+// How the aggregate pass hands u to the output pass.
+constexpr int kUNone = 0;  // not at all: the output pass evaluates again
+constexpr int kURows = 1;  // fp32, in the fp32 output rows
+constexpr int kURing = 2;  // fp16 pairs, in the ring slot p.park
+
+// L2 policies: the parked u kept before streamed data, x (read once) first out.
+OSSM_DEV uint64_t policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+OSSM_DEV uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+OSSM_DEV void st_park(uint32_t* p, uint32_t v, uint64_t pol) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.b32 [%0], %1, %2;" ::"l"(p), "r"(v), "l"(pol) : "memory");
+}
+// Drop a 128-byte line of parked u from L2 without writing it back to HBM
+// (its last reader has it in registers).
+OSSM_DEV void discard_l2(const void* p) {
+  asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
+OSSM_DEV uint32_t pack_f16x2(float2 v) {
+  const __half2 h = __floats2half2_rn(v.x, v.y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+OSSM_DEV float2 unpack_f16x2(uint32_t w) { return __half22float2(*reinterpret_cast<const __half2*>(&w)); }
 
 // w = hi + lo with hi = bf16(w) and lo = bf16(w - hi), for a pair of weights,
 // with packed conversions only (the scalar float -> bf16 conversion would
@@ -176,6 +224,8 @@ OSSM_DEV void load_mono(const Params& p, int b, int h, int lane, float2 (&m)[8])
 template <bool MONO, bool GATE>
 __global__ void __launch_bounds__(32) p3_prep_kernel(const Params p) {
   const int lane = threadIdx.x;
+  if (p.zero_ptr && blockIdx.x == 0)
+    for (int i = lane; i < p.zero_n; i += 32) p.zero_ptr[i] = 0u;
   const int nmono = MONO ? p.B * kH : 0;
   if ((int)blockIdx.x < nmono) {
     const int b = blockIdx.x / kH, h = blockIdx.x % kH;
@@ -185,6 +235,23 @@ __global__ void __launch_bounds__(32) p3_prep_kernel(const Params p) {
     float4* dst = p.cmono + (size_t)blockIdx.x * 4 * 32 + lane;
 #pragma unroll
     for (int q = 0; q < 4; ++q) dst[q * 32] = make_float4(cm[2 * q].x, cm[2 * q].y, cm[2 * q + 1].x, cm[2 * q + 1].y);
+    // the clamp-free test on both channels of every lane
+    const float* cb = p.coeffs + ((size_t)(b * kH + h) * p.Kd) * kHD + lane * 2;
+    float c0[8], c1[8];
+    float2 mono = make_float2(0.f, 0.f);
+    float sc = 1.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q, sc *= 4.f) {
+      const float2 c = q < p.K ? __ldg(reinterpret_cast<const float2*>(cb + q * kHD)) : make_float2(0.f, 0.f);
+      c0[q] = c.x;
+      c1[q] = c.y;
+      mono.x += fabsf(cm[q].x) * sc;
+      mono.y += fabsf(cm[q].y) * sc;
+    }
+    const bool cf = clamp_free_bound(gamma * clamp_free_sup(c0, p.K), mono.x) &&
+                    clamp_free_bound(gamma * clamp_free_sup(c1, p.K), mono.y);
+    const bool all = __all_sync(0xffffffffu, cf);
+    if (lane == 0 && p.noclamp) p.noclamp[blockIdx.x] = all ? 1u : 0u;
   } else if (GATE) {
     const int h = blockIdx.x - nmono;
     const int gid = lane >> 2, tig = lane & 3;
@@ -205,10 +272,85 @@ OSSM_DEV float lam_token(const Params& p, const float* lam_tok, int b, int tg, i
   return lam_tok ? __ldg(lam_tok + ((size_t)b * p.S + tg) * kH + h) : lam_base;
 }
 
+// The carries of a parked-u launch, formed at the end of the aggregate pass
+// without waiting on other CTAs: after writing its records, the CTA of chunk
+// c takes a ticket of its span; the span's last CTA (its ticket is the
+// span's chunk count less one) folds the span's records in chunk order into
+// each chunk's carry and decay product from the span start (p.carry, p.P)
+// and the span's own record (spA, spE).  It then takes a ticket of the
+// sequence; the sequence's last folds the span records in span order into
+// the state entering each span (spX).  Each writer fences before its ticket
+// and each last CTA fences after it, so it reads every record the others
+// wrote; each resets its ticket for the next slab that uses this workspace.
+// flag: one int of shared memory.
+OSSM_DEV void ring_carries(const Params& p, int b, int c, int h, int lane, int* flag) {
+  const int tid = threadIdx.x, j0 = lane * 2;
+  const int sp = c / kSpanC, c0 = sp * kSpanC, cnt = min(kSpanC, p.nchunks - c0);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) *flag = atomicAdd(p.tk_span + (size_t)b * p.nsp + sp, 1u) == (uint32_t)(cnt - 1);
+  __syncthreads();
+  if (!*flag) return;
+  __threadfence();
+  const size_t nb = (size_t)(b * kH + h) * p.nchunks + c0;
+  float2 X = make_float2(0.f, 0.f);
+  float P = 1.f;
+#pragma unroll 1
+  for (int q0 = 0; q0 < cnt; q0 += 8) {  // 8 chunk records per batch of loads
+    float a[8];
+    float2 g[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const bool in = q0 + q < cnt;
+      a[q] = in ? __ldcg(p.A + nb + q0 + q) : 1.f;
+      g[q] = in ? __ldcg(reinterpret_cast<const float2*>(p.agg + (nb + q0 + q) * kHD) + lane) : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (q0 + q < cnt) {
+        *reinterpret_cast<float2*>(p.carry + (nb + q0 + q) * kHD + j0) = X;
+        if (lane == 0) p.P[nb + q0 + q] = P;
+      }
+      X = make_float2(fmaf(a[q], X.x, g[q].x), fmaf(a[q], X.y, g[q].y));
+      P *= a[q];
+    }
+  }
+  const size_t ks = (size_t)(b * kH + h) * p.nsp;
+  *reinterpret_cast<float2*>(p.spE + (ks + sp) * kHD + j0) = X;
+  if (lane == 0) p.spA[ks + sp] = P;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    p.tk_span[(size_t)b * p.nsp + sp] = 0u;
+    *flag = atomicAdd(p.tk_seq + b, 1u) == (uint32_t)(p.nsp - 1);
+  }
+  __syncthreads();
+  if (!*flag) return;
+  __threadfence();
+  X = make_float2(0.f, 0.f);
+#pragma unroll 1
+  for (int s0 = 0; s0 < p.nsp; s0 += 8) {  // 8 span records per batch of loads
+    float sa[8];
+    float2 se[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const bool in = s0 + q < p.nsp;
+      sa[q] = in ? __ldcg(p.spA + ks + s0 + q) : 1.f;
+      se[q] = in ? __ldcg(reinterpret_cast<const float2*>(p.spE + (ks + s0 + q) * kHD) + lane) : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (s0 + q < p.nsp) *reinterpret_cast<float2*>(p.spX + (ks + s0 + q) * kHD + j0) = X;
+      X = make_float2(fmaf(sa[q], X.x, se[q].x), fmaf(sa[q], X.y, se[q].y));
+    }
+  }
+  if (tid == 0) p.tk_seq[b] = 0u;
+}
+
 // ---------------------------------------------------------------------------
 // pass 1: chunk aggregates
 // ---------------------------------------------------------------------------
-template <bool GATE, bool PRECISE, bool UC>
+template <bool GATE, bool PRECISE, int UM>
 __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
   using namespace sm100;
   extern __shared__ uint8_t smem_raw[];
@@ -226,8 +368,14 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
     mbar_init(bar, 1);
     fence_mbar_init();
     mbar_expect_tx(bar, kTile);
+    if (UM == kURing) {  // x is read once: its lines go before the parked u
+      const uint64_t pol = policy_evict_first();
 #pragma unroll
-    for (int hh = 0; hh < kH; ++hh) tma_load_3d(sm + hh * kBox, &tmap_x, bar, hh * kHD, t0, b);
+      for (int hh = 0; hh < kH; ++hh) tma_load_3d_hint(sm + hh * kBox, &tmap_x, bar, hh * kHD, t0, b, pol);
+    } else {
+#pragma unroll
+      for (int hh = 0; hh < kH; ++hh) tma_load_3d(sm + hh * kBox, &tmap_x, bar, hh * kHD, t0, b);
+    }
   }
   // while the tile lands: coefficients, gate weights (both prepared by
   // p3_prep_kernel on the fast path), the caller's decay
@@ -303,7 +451,16 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
   auto raw_t = [&](int t) {
     return *reinterpret_cast<const uint32_t*>(xs + box_off(t, lane >> 2) + (lane & 3) * 4);
   };
-  if (UC) {  // park each u in the fp32 output row it will become (tokens past the end have no row)
+  const bool nc = !PRECISE && p.noclamp && __ldg(p.noclamp + b * kH + h);  // warp-uniform
+  if (UM == kURing) {  // park each u as an fp16 pair in the ring: one 128-byte line per warp and token
+    uint32_t* up = p.park + ((size_t)(b * p.nchunks + c) * kH + h) * (kL * 32) + lane;
+    const uint64_t pol = policy_evict_last();
+    auto put = [&](int t, float2 u) { st_park(up + t * 32, pack_f16x2(u), pol); };
+    s = nc ? ema_chunk_u<PRECISE, false, false>(s, lam_s + h * kL, first, cm, gamma, raw, put)
+           : ema_chunk_u<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, put);
+    if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y))  // NaN / inf inputs: the reference's semantics
+      s = ema_chunk_u_exact<PRECISE>(s_in, lam_s + h * kL, first, cm, gamma, raw_t, put);
+  } else if (UM == kURows) {  // park each u in the fp32 output row it will become (tokens past the end have no row)
     float* uo = static_cast<float*>(p.out) + (size_t)b * p.osb + (size_t)t0 * p.oss + h * kHD + j0;
     const int nt = min(kL, p.S - t0);
     auto put = [&](int t, float2 u) {
@@ -314,7 +471,8 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
       s = ema_chunk_u_exact<PRECISE>(s_in, lam_s + h * kL, first, cm, gamma, raw_t, put);
   } else {
     auto none = [](int, float2) {};
-    s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, none);
+    s = nc ? ema_chunk<PRECISE, false, false>(s, lam_s + h * kL, first, cm, gamma, raw, none)
+           : ema_chunk<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, none);
     if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y))  // NaN / inf inputs: the reference's semantics
       s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, first, cm, gamma, raw_t, none);
   }
@@ -322,6 +480,7 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
   *reinterpret_cast<float2*>(p.agg + n * kHD + j0) = s;
   if (lane == 0) p.A[n] = a;
   if (!ok && lane == 0) atomicExch(&p.ws->status, (uint32_t)OSSM_ETIMEOUT);
+  if (UM == kURing) ring_carries(p, b, c, h, lane, reinterpret_cast<int*>(sm + kOffBar + 8));
 }
 
 // ---------------------------------------------------------------------------
@@ -617,9 +776,69 @@ __global__ void __launch_bounds__(kNT, 4) p3_outu_kernel(const Params p, const f
     *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) = make_float2(clamp1(s.x), clamp1(s.y));
 }
 
-template <bool GATE, bool PRECISE, bool UC>
+// pass 3 of a bf16-output forward from the u the aggregate pass parked as fp16
+// pairs in the ring (kURing): no second evaluation and no second read of x.
+// Each lane loads its 32 u words first (one 128-byte line per warp and
+// token, still in L2), then the chunk's entry state (its span's entry state
+// carried through the span, both formed by the aggregate pass) and decays,
+// runs the EMA and writes the outputs; then each lane drops one of the
+// warp's lines from L2, so the parked u never goes to HBM.  The final state
+// is the chunk's aggregate applied to its entry state in fp32 (A X + agg),
+// so it does not carry the fp16 rounding of u.
+__global__ void __launch_bounds__(kNT, 4) p3_outp_kernel(const Params p, const float* lam_tok) {
+  __shared__ float2 lam_s[kH * kL];
+  const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
+  const int j0 = lane * 2, ch0 = h * kHD + j0;
+  const int c = (int)(blockIdx.x / p.B), b = (int)(blockIdx.x % p.B);
+  const int t0 = c * kL, nt = min(kL, p.S - t0);
+  const size_t n = (size_t)(b * kH + h) * p.nchunks + c;
+  const uint32_t* up = p.park + ((size_t)(b * p.nchunks + c) * kH + h) * (kL * 32);
+  uint32_t r[kL];
+#pragma unroll
+  for (int t = 0; t < kL; ++t) r[t] = __ldcg(up + t * 32 + lane);
+  const bool first = c == 0 && p.starts_seq;
+  float2 X;  // the state entering the chunk: from its span's entry state and the in-span carry
+  if (first) {
+    X = p.init ? __ldg(reinterpret_cast<const float2*>(p.init + (size_t)b * kD + ch0)) : make_float2(0.f, 0.f);
+  } else {
+    const float2 Xs = *reinterpret_cast<const float2*>(p.spX + ((size_t)(b * kH + h) * p.nsp + c / kSpanC) * kHD + j0);
+    const float2 Cl = *reinterpret_cast<const float2*>(p.carry + n * kHD + j0);
+    const float Pl = p.P[n];
+    X = make_float2(fmaf(Pl, Xs.x, Cl.x), fmaf(Pl, Xs.y, Cl.y));
+  }
+  const float lam_base = p.lam_h ? __ldg(p.lam_h + h) : p.momentum;
+  const float lam = lam_token(p, lam_tok, b, t0 + lane, h, lam_base);
+  lam_s[h * kL + lane] = make_float2(lam, 1.f - lam);
+  __syncwarp();
+  const float2* lm = lam_s + h * kL;
+  __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)b * p.osb + (size_t)t0 * kD + ch0;
+  float2 s = X;
+  if (nt == kL) {
+#pragma unroll
+    for (int t = 0; t < kL; ++t) {
+      s = ema_step(s, lm[t], unpack_f16x2(r[t]), t == 0 && first);
+      st2(op + t * kD, s);
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < kL; ++t) {
+      s = ema_step(s, lm[t], unpack_f16x2(r[t]), t == 0 && first);
+      if (t < nt) st2(op + t * kD, s);
+    }
+  }
+  __syncwarp();  // every lane holds its words of all 32 lines
+  discard_l2(up + lane * 32);
+  if (p.fin && t0 + kL >= p.S) {  // decays are 1 past the end, so A X + agg is the sequence's final state
+    const float An = p.A[n];
+    const float2 E = *reinterpret_cast<const float2*>(p.agg + n * kHD + j0);
+    *reinterpret_cast<float2*>(p.fin + (size_t)b * kD + ch0) =
+        make_float2(clamp1(fmaf(An, X.x, E.x)), clamp1(fmaf(An, X.y, E.y)));
+  }
+}
+
+template <bool GATE, bool PRECISE, int UM>
 cudaError_t launch_agg(const CUtensorMap& mx, const Params& p, cudaStream_t st) {
-  auto kern = p3_agg_kernel<GATE, PRECISE, UC>;
+  auto kern = p3_agg_kernel<GATE, PRECISE, UM>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAggSmem);
   if (e != cudaSuccess) return e;
   kern<<<p.B * p.nchunks, kNT, kAggSmem, st>>>(mx, p);
@@ -655,6 +874,7 @@ size_t p3_single_bytes(const ossm_fwd_args* a) {
   size_t bytes = p3_al(sizeof(WsHeader)) + 2 * p3_al(N * 4) + 2 * p3_al(N * p3::kHD * 4) + 2 * p3_al(NB * 4) +
                  2 * p3_al(NB * p3::kHD * 4);
   bytes += p3_al((size_t)a->B * p3::kH * 4 * 32 * 16) + p3_al((size_t)p3::kH * 4 * 32 * 16);  // cmono, wfrag
+  bytes += p3_al((size_t)a->B * p3::kH * 4);                                                     // noclamp
   bytes += p3_al((size_t)a->B * p3::kD * 4);  // the state entering a shard (sequence-sharded calls)
   if (a->gate_w && !a->lam_tok) bytes += p3_al((size_t)a->B * a->S * p3::kH * 4);
   return bytes;
@@ -663,7 +883,7 @@ size_t p3_single_bytes(const ossm_fwd_args* a) {
 // A batch runs as kGroups groups of whole sequences on kStreams streams when
 // every group still fills the GPU for about two waves of the streaming
 // kernels (ossm_p3_launch), else as one launch.
-constexpr int kGroups = 2, kStreams = 2;
+constexpr int kGroups = 2, kStreams = 5;
 int p3_groups(const ossm_fwd_args* a) {
   if (a->flags & OSSM_F_ONE_STREAM) return 1;
   const long long nch = (a->S + p3::kL - 1) / p3::kL;
@@ -708,10 +928,65 @@ ossm_fwd_args p3_tokens(const ossm_fwd_args* a, int s0, int s1) {
   return h;
 }
 
+// bf16 outputs with u parked in L2 (kURing): the batch runs as slabs of whole
+// sequences, slab k on stream k % kParkStreams, two launches each (the
+// aggregate pass, which also forms the carries, and the output pass).  Each
+// stream has its own workspace region and ring slot, which its next slab
+// reuses once its output pass is done (a stream's launches run in order), so
+// at most kParkStreams slabs of parked u are live: with slabs of about 16 MB,
+// 84 MB of the 126 MB L2, held there by an evict-last policy while x (loaded
+// evict-first) and the outputs stream past, and dropped by the output pass
+// without a write-back.  Measured at config 2 (gated step under graph
+// replay): 2 streams 144 us, 3 125, 4 115, 5 109, 6 114, 8 114, against
+// 120.6 us for the re-evaluating path.
+constexpr size_t kParkSeqMax = 24u << 20;  // a sequence's parked u must fit this
+constexpr size_t kParkSlab = 16u << 20;    // target parked u per slab
+constexpr int kParkStreams = 5;            // streams, ring slots and workspace regions
+static_assert(kParkStreams <= kStreams, "park streams");
+size_t p3_park_seq_bytes(const ossm_fwd_args* a) {
+  return (size_t)((a->S + p3::kL - 1) / p3::kL) * p3::kL * p3::kD * 2;
+}
+int p3_park_nsp(const ossm_fwd_args* a) {
+  const int nch = (a->S + p3::kL - 1) / p3::kL;
+  return (nch + p3::kSpanC - 1) / p3::kSpanC;
+}
+// Sequences per slab, or 0 when this mode does not apply: the bf16 fast
+// path with outputs contiguous along tokens, and sequences whose parked u
+// fits.  Not under OSSM_F_ONE_STREAM (the no-allocation entry point's fixed
+// scratch has no room for the ring).
+int p3_park_slab(const ossm_fwd_args* a) {
+  if (a->flags & (OSSM_F_ONE_STREAM | OSSM_F_PRECISE)) return 0;
+  if (a->out_dtype != OSSM_BF16 || a->out_stride_s != p3::kD) return 0;
+  const size_t seq = p3_park_seq_bytes(a);
+  if (seq > kParkSeqMax) return 0;
+  return (int)std::max<size_t>(1, std::min<size_t>((size_t)a->B, kParkSlab / seq));
+}
+int p3_park_nstreams(const ossm_fwd_args* a, int sb) { return std::min((a->B + sb - 1) / sb, kParkStreams); }
+// Front: header, every sequence's coefficients and clamp flags, the gate
+// fragments, and the tickets of every stream's region (cleared by the setup
+// kernel).
+size_t p3_park_ticket_words(const ossm_fwd_args* a, int sb) { return (size_t)sb * (p3_park_nsp(a) + 1); }
+size_t p3_park_front_bytes(const ossm_fwd_args* a, int sb) {
+  return p3_al(sizeof(WsHeader)) + p3_al((size_t)a->B * p3::kH * 4 * 32 * 16) + p3_al((size_t)p3::kH * 4 * 32 * 16) +
+         p3_al((size_t)a->B * p3::kH * 4) + p3_al((size_t)p3_park_nstreams(a, sb) * p3_park_ticket_words(a, sb) * 4);
+}
+// One stream's region: the slab's three-pass workspace, its ring slot, and
+// the span records (spA, spE, spX).
+size_t p3_park_stream_bytes(const ossm_fwd_args* a, int sb) {
+  const ossm_fwd_args h = p3_rows(a, 0, sb);
+  const size_t nsp = (size_t)sb * p3::kH * p3_park_nsp(a);
+  return p3_al(p3_single_bytes(&h)) + p3_al((size_t)sb * p3_park_seq_bytes(a)) + p3_al(nsp * 4) +
+         2 * p3_al(nsp * p3::kHD * 4);
+}
+size_t p3_park_bytes(const ossm_fwd_args* a, int sb) {
+  return p3_park_front_bytes(a, sb) + (size_t)p3_park_nstreams(a, sb) * p3_park_stream_bytes(a, sb);
+}
+
 }  // namespace
 
 size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a) {
   size_t bytes = p3_single_bytes(a);
+  if (const int sb = p3_park_slab(a)) bytes = std::max(bytes, p3_park_bytes(a, sb));
   const int G = p3_groups(a);
   if (G > 1) {
     size_t sum = 0;
@@ -783,6 +1058,8 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
   off += al((size_t)a->B * kH * 4 * 32 * 16);
   p.wfrag = reinterpret_cast<uint4*>(ws + off);
   off += al((size_t)kH * 4 * 32 * 16);
+  p.noclamp = reinterpret_cast<uint32_t*>(ws + off);
+  off += al((size_t)a->B * kH * 4);
   p.shard_carry = reinterpret_cast<float*>(ws + off);
   off += al((size_t)a->B * kD * 4);
   p.lam_ws = gate ? reinterpret_cast<float*>(ws + off) : nullptr;
@@ -791,6 +1068,12 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
   p.tot_E = nullptr;
   p.carry_in = nullptr;
   p.uc = 0;
+  p.park = nullptr;
+  p.nsp = 0;
+  p.tk_span = p.tk_seq = nullptr;
+  p.spA = p.spE = p.spX = nullptr;
+  p.zero_ptr = nullptr;
+  p.zero_n = 0;
   if ((long long)a->B * p.nchunks > 0x7fffffffLL || (long long)a->B * kH * p.nblk > 0x7fffffffLL) return OSSM_EINVAL;
   return OSSM_OK;
 }
@@ -816,15 +1099,15 @@ int p3_uc_mode(const ossm_fwd_args* a) {
   return (size_t)a->B * a->S * D * 4 <= (64u << 20) ? 1 : 0;
 }
 
-// pass 1: aggregates
-int p3_aggregates(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
+// pass 1: aggregates (with the per-launch setup unless the caller ran it)
+int p3_aggregates(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st, bool prep = true) {
   using namespace p3;
   CUtensorMap mx;
   if (!fast::encode_map(&mx, a->x, a->S, a->B, a->x_stride_s, a->x_stride_b, kL)) return OSSM_EINVAL;
   const bool gate = a->gate_w && !a->lam_tok;
   const bool precise = (a->out_dtype == OSSM_F32) || (a->flags & OSSM_F_PRECISE);
   const int nprep = (precise ? 0 : a->B * kH) + (gate ? kH : 0);
-  if (nprep > 0) {
+  if (prep && nprep > 0) {
     if (precise)
       p3_prep_kernel<false, true><<<nprep, 32, 0, st>>>(p);
     else if (gate)
@@ -834,11 +1117,13 @@ int p3_aggregates(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) 
   }
   cudaError_t e;
   if (p.uc)
-    e = gate ? launch_agg<true, true, true>(mx, p, st) : launch_agg<false, true, true>(mx, p, st);
+    e = gate ? launch_agg<true, true, kURows>(mx, p, st) : launch_agg<false, true, kURows>(mx, p, st);
+  else if (p.park)  // the bf16 fast path only
+    e = gate ? launch_agg<true, false, kURing>(mx, p, st) : launch_agg<false, false, kURing>(mx, p, st);
   else if (precise)
-    e = gate ? launch_agg<true, true, false>(mx, p, st) : launch_agg<false, true, false>(mx, p, st);
+    e = gate ? launch_agg<true, true, kUNone>(mx, p, st) : launch_agg<false, true, kUNone>(mx, p, st);
   else
-    e = gate ? launch_agg<true, false, false>(mx, p, st) : launch_agg<false, false, false>(mx, p, st);
+    e = gate ? launch_agg<true, false, kUNone>(mx, p, st) : launch_agg<false, false, kUNone>(mx, p, st);
   return e == cudaSuccess ? OSSM_OK : OSSM_ELAUNCH;
 }
 
@@ -865,6 +1150,9 @@ int p3_back(const ossm_fwd_args* a, const p3::Params& p, cudaStream_t st) {
   cudaError_t e;
   if (p.uc) {
     p3_outu_kernel<<<p.B * p.nchunks, kNT, 0, st>>>(p, lam_tok);
+    e = cudaGetLastError();
+  } else if (p.park) {
+    p3_outp_kernel<<<p.B * p.nchunks, kNT, 0, st>>>(p, lam_tok);
     e = cudaGetLastError();
   } else if (a->out_dtype == OSSM_F32)
     e = launch_out<true, float>(p, lam_tok, st);
@@ -913,8 +1201,9 @@ int p3_launch_split(const ossm_fwd_args* a, int G, char* ws, cudaStream_t st) {
   cudaStream_t streams[kStreams];
   streams[0] = st;
   for (int k = 1; k < kStreams; ++k) streams[k] = sd.s[k];
+  const int ns = std::min(G, kStreams);
   bool ok = cudaEventRecord(sd.fork, st) == cudaSuccess;
-  for (int k = 1; k < kStreams; ++k) ok = ok && cudaStreamWaitEvent(sd.s[k], sd.fork, 0) == cudaSuccess;
+  for (int k = 1; k < ns; ++k) ok = ok && cudaStreamWaitEvent(sd.s[k], sd.fork, 0) == cudaSuccess;
   int r = ok ? OSSM_OK : OSSM_ELAUNCH;
   WsHeader* header = reinterpret_cast<WsHeader*>(ws);
   size_t off = 0;
@@ -926,12 +1215,12 @@ int p3_launch_split(const ossm_fwd_args* a, int G, char* ws, cudaStream_t st) {
     if (r != OSSM_OK) break;
     p.ws = header;  // one header: the sticky status lives at the workspace start
     p.uc = p3_uc_mode(&h);
-    r = p3_front(&h, p, streams[g % kStreams]);
-    if (r == OSSM_OK) r = p3_back(&h, p, streams[g % kStreams]);
+    r = p3_front(&h, p, streams[g % ns]);
+    if (r == OSSM_OK) r = p3_back(&h, p, streams[g % ns]);
   }
   // join, also after an error, so the caller's later work never overlaps
   bool joined = true;
-  for (int k = 1; k < kStreams; ++k)
+  for (int k = 1; k < ns; ++k)
     joined = joined && cudaEventRecord(sd.join[k], sd.s[k]) == cudaSuccess &&
              cudaStreamWaitEvent(st, sd.join[k], 0) == cudaSuccess;
   if (r != OSSM_OK) return r;
@@ -982,9 +1271,101 @@ int p3_launch_seq_split(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
   return ok && joined ? OSSM_OK : OSSM_ELAUNCH;
 }
 
+// The parked-u forward (kURing): the per-launch setup once for the whole
+// batch on the caller's stream (also clearing the tickets), then the slabs,
+// forked onto the streams.  One slab runs on the caller's stream alone.
+int p3_launch_park(const ossm_fwd_args* a, int sb, char* ws, cudaStream_t st) {
+  using namespace p3;
+  const int nslab = (a->B + sb - 1) / sb;
+  const int ns = p3_park_nstreams(a, sb);
+  P3Side* sd = nullptr;
+  std::unique_lock<std::mutex> lock;
+  if (ns > 1) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return OSSM_ELAUNCH;
+    sd = &g_p3side[dev];
+    lock = std::unique_lock<std::mutex>(sd->mu);
+    if (!p3_side_ready(*sd)) return OSSM_ELAUNCH;
+  }
+  const int nsp = p3_park_nsp(a);
+  size_t off = p3_al(sizeof(WsHeader));
+  WsHeader* header = reinterpret_cast<WsHeader*>(ws);
+  float4* cmono = reinterpret_cast<float4*>(ws + off);
+  off += p3_al((size_t)a->B * kH * 4 * 32 * 16);
+  uint4* wfrag = reinterpret_cast<uint4*>(ws + off);
+  off += p3_al((size_t)kH * 4 * 32 * 16);
+  uint32_t* noclamp = reinterpret_cast<uint32_t*>(ws + off);
+  off += p3_al((size_t)a->B * kH * 4);
+  uint32_t* tickets = reinterpret_cast<uint32_t*>(ws + off);
+  const size_t tw = p3_park_ticket_words(a, sb);
+  const ossm_fwd_args h0 = p3_rows(a, 0, sb);
+  const size_t front = p3_park_front_bytes(a, sb), per = p3_park_stream_bytes(a, sb);
+  const size_t ring_off = p3_al(p3_single_bytes(&h0));
+  const size_t spa_off = ring_off + p3_al((size_t)sb * p3_park_seq_bytes(a));
+  const size_t nspw = (size_t)sb * kH * nsp;
+  const bool gate = a->gate_w && !a->lam_tok;
+  {  // the setup of every slab at once
+    Params pp;
+    int r = p3_params(&h0, ws + front, pp);
+    if (r != OSSM_OK) return r;
+    pp.B = a->B;
+    pp.coeffs = a->coeffs;
+    pp.cmono = cmono;
+    pp.wfrag = wfrag;
+    pp.noclamp = noclamp;
+    pp.zero_ptr = tickets;
+    pp.zero_n = (int)(ns * tw);
+    const int nprep = a->B * kH + (gate ? kH : 0);
+    if (gate)
+      p3_prep_kernel<true, true><<<nprep, 32, 0, st>>>(pp);
+    else
+      p3_prep_kernel<true, false><<<nprep, 32, 0, st>>>(pp);
+    if (cudaGetLastError() != cudaSuccess) return OSSM_ELAUNCH;
+  }
+  cudaStream_t streams[kStreams];
+  streams[0] = st;
+  bool ok = true;
+  if (sd) {
+    for (int k = 1; k < ns; ++k) streams[k] = sd->s[k];
+    ok = cudaEventRecord(sd->fork, st) == cudaSuccess;
+    for (int k = 1; k < ns; ++k) ok = ok && cudaStreamWaitEvent(sd->s[k], sd->fork, 0) == cudaSuccess;
+  }
+  int r = ok ? OSSM_OK : OSSM_ELAUNCH;
+  for (int k = 0; k < nslab && r == OSSM_OK; ++k) {
+    const int b0 = k * sb, b1 = std::min(a->B, b0 + sb), si = k % ns;
+    const ossm_fwd_args h = p3_rows(a, b0, b1);
+    char* region = ws + front + (size_t)si * per;
+    Params p;
+    r = p3_params(&h, region, p);
+    if (r != OSSM_OK) break;
+    p.ws = header;  // one header: the sticky status lives at the workspace start
+    p.cmono = cmono + (size_t)b0 * kH * 4 * 32;
+    p.wfrag = wfrag;
+    p.noclamp = noclamp + (size_t)b0 * kH;
+    p.park = reinterpret_cast<uint32_t*>(region + ring_off);
+    p.nsp = nsp;
+    p.tk_span = tickets + (size_t)si * tw;
+    p.tk_seq = p.tk_span + (size_t)sb * nsp;
+    p.spA = reinterpret_cast<float*>(region + spa_off);
+    p.spE = reinterpret_cast<float*>(region + spa_off + p3_al(nspw * 4));
+    p.spX = reinterpret_cast<float*>(region + spa_off + p3_al(nspw * 4) + p3_al(nspw * kHD * 4));
+    r = p3_aggregates(&h, p, streams[si], false);
+    if (r == OSSM_OK) r = p3_back(&h, p, streams[si]);
+  }
+  // join, also after an error, so the caller's later work never overlaps
+  bool joined = true;
+  if (sd)
+    for (int k = 1; k < ns; ++k)
+      joined = joined && cudaEventRecord(sd->join[k], sd->s[k]) == cudaSuccess &&
+               cudaStreamWaitEvent(st, sd->join[k], 0) == cudaSuccess;
+  if (r != OSSM_OK) return r;
+  return ok && joined ? OSSM_OK : OSSM_ELAUNCH;
+}
+
 }  // namespace
 
 int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
+  if (const int sb = p3_park_slab(a)) return p3_launch_park(a, sb, ws, st);
   const int G = p3_groups(a);
   if (G > 1) return p3_launch_split(a, G, ws, st);
   if (p3_seq_split(a)) return p3_launch_seq_split(a, ws, st);

@@ -56,6 +56,15 @@ OSSM_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int 
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+// The same with an L2 cache policy (createpolicy) for the source lines.
+OSSM_DEV void tma_load_3d_hint(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+      "l"(pol)
+      : "memory");
+}
 // 1D bulk copy global -> shared (16-byte aligned, size a multiple of 16),
 // completing on an mbarrier transaction count (CTA-local destination).
 OSSM_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
