@@ -108,10 +108,7 @@ OSSM_DEV float eval_u1(float x, const float2 (&m)[8], bool second, float gamma) 
 }
 // Both channels of one token.  The fast path runs its Horner on the channel
 // pair with packed fp32x2 FMAs (one instruction per degree for two channels).
-// CLAMP = false drops the clamp to +-4 on the fast path, for coefficients
-// whose polynomial provably stays inside it (clamp_free_bound): the clamp is
-// then the identity on every value Horner can produce, NaN included.
-template <bool PRECISE, bool EXACT, bool CLAMP = true>
+template <bool PRECISE, bool EXACT>
 OSSM_DEV float2 eval_u(uint32_t raw, const float2 (&m)[8], float gamma) {
   const float x0 = __uint_as_float(raw << 16), x1 = __uint_as_float(raw & 0xffff0000u);
   if (!PRECISE && !EXACT) {
@@ -120,42 +117,9 @@ OSSM_DEV float2 eval_u(uint32_t raw, const float2 (&m)[8], float gamma) {
     float2 y = m[7];
 #pragma unroll
     for (int q = 6; q >= 0; --q) y = fma2(y, z, m[q]);
-    if (!CLAMP) return make_float2(tanh_fast(y.x), tanh_fast(y.y));
     return make_float2(tanh_fast(clamp4_nan(y.x)), tanh_fast(clamp4_nan(y.y)));
   }
   return make_float2(eval_u1<PRECISE, EXACT>(x0, m, false, gamma), eval_u1<PRECISE, EXACT>(x1, m, true, gamma));
-}
-
-// Whether the fast path may drop the clamp for one channel.  bound: the
-// largest |gamma y(xn)| over |xn| <= 1 (clamp_free_sup); mono = gamma sum |a_k|
-// of the monomial form (unscaled).  Horner on that form adds at most 14
-// roundings of terms summing to mono, and the conversion to it a few more:
-// under 1.5e-3 while mono <= 1000.  So the computed y stays below
-// 3.9 + 1.5e-3 < 4 and the clamp is the identity on it.  NaN coefficients
-// fail the comparisons and keep the clamp.
-OSSM_DEV bool clamp_free_bound(float bound, float mono) { return bound <= 3.9f && mono <= 1000.f; }
-
-// An upper bound of max |sum_k c_k T_k(xn)| over |xn| <= 1 for the first K
-// of 8 raw coefficients: the largest value at the 32 zeros of T_32 times
-// 1 / cos(7 pi / 64) (Ehlich and Zeller: for a polynomial of degree n and
-// m > n such nodes, the maximum over [-1, 1] is at most the nodes' maximum
-// over cos(n pi / 2m)), widened by 1% for the fp32 nodes and Clenshaw.
-OSSM_DEV float clamp_free_sup(const float (&c)[8], int K) {
-  float mx = 0.f;
-#pragma unroll 4
-  for (int j = 0; j < 32; ++j) {
-    const float xn = cospif((float)(2 * j + 1) * (1.f / 64.f));
-    const float x2 = 2.f * xn;
-    float u1 = 0.f, u2 = 0.f;
-#pragma unroll
-    for (int q = 7; q >= 1; --q) {
-      const float t = fmaf(x2, u1, (q < K ? c[q] : 0.f) - u2);
-      u2 = u1;
-      u1 = t;
-    }
-    mx = fmaxf(mx, fabsf(fmaf(xn, u1, (K > 0 ? c[0] : 0.f) - u2)));
-  }
-  return mx * (1.0621f * 1.01f) + 1e-6f;
 }
 
 OSSM_DEV float clamp1_nan(float v) {  // NaN-propagating clamp to [-1, 1]
@@ -174,12 +138,12 @@ OSSM_DEV float2 ema_step(float2 s, float2 lm, float2 u, bool first) {  // lm = (
 
 // The 32-token EMA of one chunk from state s (decays lam[0..31]); RAW(t) gives
 // the packed bf16 pair of token t, OUT(t, s) receives each state.
-template <bool PRECISE, bool EXACT, bool CLAMP = true, typename RawF, typename OutF>
+template <bool PRECISE, bool EXACT, typename RawF, typename OutF>
 OSSM_DEV float2 ema_chunk(float2 s, const float2* lam, bool first, const float2 (&m)[8], float gamma, RawF raw,
                           OutF out) {
 #pragma unroll
   for (int t = 0; t < kL; ++t) {
-    s = ema_step(s, lam[t], eval_u<PRECISE, EXACT, CLAMP>(raw(t), m, gamma), t == 0 && first);
+    s = ema_step(s, lam[t], eval_u<PRECISE, EXACT>(raw(t), m, gamma), t == 0 && first);
     out(t, s);
   }
   return s;
@@ -199,12 +163,12 @@ OSSM_DEV float2 ema_chunk_exact(float2 s, const float2* lam, bool first, const f
 
 // The same two loops, handing each token's u to U(t, u) as well (the
 // aggregate pass parks u for the output pass).
-template <bool PRECISE, bool EXACT, bool CLAMP = true, typename RawF, typename UF>
+template <bool PRECISE, bool EXACT, typename RawF, typename UF>
 OSSM_DEV float2 ema_chunk_u(float2 s, const float2* lam, bool first, const float2 (&m)[8], float gamma, RawF raw,
                             UF uf) {
 #pragma unroll
   for (int t = 0; t < kL; ++t) {
-    const float2 u = eval_u<PRECISE, EXACT, CLAMP>(raw(t), m, gamma);
+    const float2 u = eval_u<PRECISE, EXACT>(raw(t), m, gamma);
     uf(t, u);
     s = ema_step(s, lam[t], u, t == 0 && first);
   }

@@ -125,7 +125,6 @@ struct Params {
   const float* lam_in;  // caller's per-token decay [B,S,H] or NULL
   float* lam_ws;        // per-token decays written by the gate [B,S,H] (workspace)
   float4* cmono;        // [B*8][4][32]: each lane's gamma-folded, 4^-k-scaled monomial coefficients
-  uint32_t* noclamp;    // [B*8]: 1 where the head's polynomial stays inside the clamp (clamp_free_bound)
   uint4* wfrag;         // [8][4][32]: each lane's mma B fragments of the gate weights, bf16 hi + lo
   const float* init;
   float* fin;
@@ -235,23 +234,6 @@ __global__ void __launch_bounds__(32) p3_prep_kernel(const Params p) {
     float4* dst = p.cmono + (size_t)blockIdx.x * 4 * 32 + lane;
 #pragma unroll
     for (int q = 0; q < 4; ++q) dst[q * 32] = make_float4(cm[2 * q].x, cm[2 * q].y, cm[2 * q + 1].x, cm[2 * q + 1].y);
-    // the clamp-free test on both channels of every lane
-    const float* cb = p.coeffs + ((size_t)(b * kH + h) * p.Kd) * kHD + lane * 2;
-    float c0[8], c1[8];
-    float2 mono = make_float2(0.f, 0.f);
-    float sc = 1.f;
-#pragma unroll
-    for (int q = 0; q < 8; ++q, sc *= 4.f) {
-      const float2 c = q < p.K ? __ldg(reinterpret_cast<const float2*>(cb + q * kHD)) : make_float2(0.f, 0.f);
-      c0[q] = c.x;
-      c1[q] = c.y;
-      mono.x += fabsf(cm[q].x) * sc;
-      mono.y += fabsf(cm[q].y) * sc;
-    }
-    const bool cf = clamp_free_bound(gamma * clamp_free_sup(c0, p.K), mono.x) &&
-                    clamp_free_bound(gamma * clamp_free_sup(c1, p.K), mono.y);
-    const bool all = __all_sync(0xffffffffu, cf);
-    if (lane == 0 && p.noclamp) p.noclamp[blockIdx.x] = all ? 1u : 0u;
   } else if (GATE) {
     const int h = blockIdx.x - nmono;
     const int gid = lane >> 2, tig = lane & 3;
@@ -451,13 +433,11 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
   auto raw_t = [&](int t) {
     return *reinterpret_cast<const uint32_t*>(xs + box_off(t, lane >> 2) + (lane & 3) * 4);
   };
-  const bool nc = !PRECISE && p.noclamp && __ldg(p.noclamp + b * kH + h);  // warp-uniform
   if (UM == kURing) {  // park each u as an fp16 pair in the ring: one 128-byte line per warp and token
     uint32_t* up = p.park + ((size_t)(b * p.nchunks + c) * kH + h) * (kL * 32) + lane;
     const uint64_t pol = policy_evict_last();
     auto put = [&](int t, float2 u) { st_park(up + t * 32, pack_f16x2(u), pol); };
-    s = nc ? ema_chunk_u<PRECISE, false, false>(s, lam_s + h * kL, first, cm, gamma, raw, put)
-           : ema_chunk_u<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, put);
+    s = ema_chunk_u<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, put);
     if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y))  // NaN / inf inputs: the reference's semantics
       s = ema_chunk_u_exact<PRECISE>(s_in, lam_s + h * kL, first, cm, gamma, raw_t, put);
   } else if (UM == kURows) {  // park each u in the fp32 output row it will become (tokens past the end have no row)
@@ -471,8 +451,7 @@ __global__ void __launch_bounds__(kNT, 4) p3_agg_kernel(const __grid_constant__ 
       s = ema_chunk_u_exact<PRECISE>(s_in, lam_s + h * kL, first, cm, gamma, raw_t, put);
   } else {
     auto none = [](int, float2) {};
-    s = nc ? ema_chunk<PRECISE, false, false>(s, lam_s + h * kL, first, cm, gamma, raw, none)
-           : ema_chunk<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, none);
+    s = ema_chunk<PRECISE, false>(s, lam_s + h * kL, first, cm, gamma, raw, none);
     if (__any_sync(0xffffffffu, s.x != s.x || s.y != s.y))  // NaN / inf inputs: the reference's semantics
       s = ema_chunk_exact<PRECISE>(s_in, lam_s + h * kL, first, cm, gamma, raw_t, none);
   }
@@ -874,7 +853,6 @@ size_t p3_single_bytes(const ossm_fwd_args* a) {
   size_t bytes = p3_al(sizeof(WsHeader)) + 2 * p3_al(N * 4) + 2 * p3_al(N * p3::kHD * 4) + 2 * p3_al(NB * 4) +
                  2 * p3_al(NB * p3::kHD * 4);
   bytes += p3_al((size_t)a->B * p3::kH * 4 * 32 * 16) + p3_al((size_t)p3::kH * 4 * 32 * 16);  // cmono, wfrag
-  bytes += p3_al((size_t)a->B * p3::kH * 4);                                                     // noclamp
   bytes += p3_al((size_t)a->B * p3::kD * 4);  // the state entering a shard (sequence-sharded calls)
   if (a->gate_w && !a->lam_tok) bytes += p3_al((size_t)a->B * a->S * p3::kH * 4);
   return bytes;
@@ -962,13 +940,12 @@ int p3_park_slab(const ossm_fwd_args* a) {
   return (int)std::max<size_t>(1, std::min<size_t>((size_t)a->B, kParkSlab / seq));
 }
 int p3_park_nstreams(const ossm_fwd_args* a, int sb) { return std::min((a->B + sb - 1) / sb, kParkStreams); }
-// Front: header, every sequence's coefficients and clamp flags, the gate
-// fragments, and the tickets of every stream's region (cleared by the setup
+// Front: header, every sequence's coefficients, the gate fragments, and the tickets of every stream's region (cleared by the setup
 // kernel).
 size_t p3_park_ticket_words(const ossm_fwd_args* a, int sb) { return (size_t)sb * (p3_park_nsp(a) + 1); }
 size_t p3_park_front_bytes(const ossm_fwd_args* a, int sb) {
   return p3_al(sizeof(WsHeader)) + p3_al((size_t)a->B * p3::kH * 4 * 32 * 16) + p3_al((size_t)p3::kH * 4 * 32 * 16) +
-         p3_al((size_t)a->B * p3::kH * 4) + p3_al((size_t)p3_park_nstreams(a, sb) * p3_park_ticket_words(a, sb) * 4);
+         p3_al((size_t)p3_park_nstreams(a, sb) * p3_park_ticket_words(a, sb) * 4);
 }
 // One stream's region: the slab's three-pass workspace, its ring slot, and
 // the span records (spA, spE, spX).
@@ -1058,8 +1035,6 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
   off += al((size_t)a->B * kH * 4 * 32 * 16);
   p.wfrag = reinterpret_cast<uint4*>(ws + off);
   off += al((size_t)kH * 4 * 32 * 16);
-  p.noclamp = reinterpret_cast<uint32_t*>(ws + off);
-  off += al((size_t)a->B * kH * 4);
   p.shard_carry = reinterpret_cast<float*>(ws + off);
   off += al((size_t)a->B * kD * 4);
   p.lam_ws = gate ? reinterpret_cast<float*>(ws + off) : nullptr;
@@ -1294,8 +1269,6 @@ int p3_launch_park(const ossm_fwd_args* a, int sb, char* ws, cudaStream_t st) {
   off += p3_al((size_t)a->B * kH * 4 * 32 * 16);
   uint4* wfrag = reinterpret_cast<uint4*>(ws + off);
   off += p3_al((size_t)kH * 4 * 32 * 16);
-  uint32_t* noclamp = reinterpret_cast<uint32_t*>(ws + off);
-  off += p3_al((size_t)a->B * kH * 4);
   uint32_t* tickets = reinterpret_cast<uint32_t*>(ws + off);
   const size_t tw = p3_park_ticket_words(a, sb);
   const ossm_fwd_args h0 = p3_rows(a, 0, sb);
@@ -1312,7 +1285,6 @@ int p3_launch_park(const ossm_fwd_args* a, int sb, char* ws, cudaStream_t st) {
     pp.coeffs = a->coeffs;
     pp.cmono = cmono;
     pp.wfrag = wfrag;
-    pp.noclamp = noclamp;
     pp.zero_ptr = tickets;
     pp.zero_n = (int)(ns * tw);
     const int nprep = a->B * kH + (gate ? kH : 0);
@@ -1341,7 +1313,6 @@ int p3_launch_park(const ossm_fwd_args* a, int sb, char* ws, cudaStream_t st) {
     p.ws = header;  // one header: the sticky status lives at the workspace start
     p.cmono = cmono + (size_t)b0 * kH * 4 * 32;
     p.wfrag = wfrag;
-    p.noclamp = noclamp + (size_t)b0 * kH;
     p.park = reinterpret_cast<uint32_t*>(region + ring_off);
     p.nsp = nsp;
     p.tk_span = tickets + (size_t)si * tw;
