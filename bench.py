@@ -286,17 +286,27 @@ def run_ours(args):
         step(0)
         step(1)
     torch.cuda.synchronize()
-    # the kernels this step runs: the grouped single-evaluation kernel (one
-    # launch), or the three-pass kernels (p3_prep, p3_agg, p3_carry, p3_out per
-    # group of sequences; a batch whose halves each hold >= 1024 (sequence,
-    # 32-token chunk) units runs as two halves on two streams)
+    # the kernels this step runs: the parked three-pass kernels (bf16 outputs:
+    # p3_prep once, then per slab of sequences p3_agg, which parks u in L2 as
+    # fp16 and forms the carries, and p3_outp, which reads u back; slabs of
+    # about 16 MB of u on up to 5 streams), the three-pass kernels (p3_prep,
+    # p3_agg, p3_carry, p3_out per group of sequences), or the grouped
+    # single-evaluation kernel (one launch)
     path = O.forward_path(xs[0], c, lambda_per_head=lam, gate_weight=W, gate_bias=bvec, init_state=init)
+    seq_u = ((S + 31) // 32) * 32 * D * 2
+    slab = max(1, min(B, (16 << 20) // seq_u))
+    nslab = (B + slab - 1) // slab
     groups = 2 if B >= 2 and (B // 2) * ((S + 31) // 32) >= 1024 else 1
-    launches_per_step = 1 if path == "grouped" else 4 * groups
+    launches_per_step = {"grouped": 1, "parked": 1 + 2 * nslab}.get(path, 4 * groups)
+    eval_passes = 1 if path in ("grouped", "parked") else 2  # evaluations of each element per step
     kernel_label = ("grp_fwd_kernel: one CTA per SM, each sequence owned by a group of CTAs, every element "
                     "evaluated once, local states parked in TMEM, tile aggregates exchanged through a ring in "
                     "global memory two rounds deep"
                     if path == "grouped" else
+                    f"forward step: p3_prep_kernel + {nslab} slabs of {slab} sequence(s) on up to 5 streams, each "
+                    "p3_agg_kernel (gate, u evaluated once and parked in L2 as fp16, chunk aggregates, carries by "
+                    "span and sequence tickets) + p3_outp_kernel (EMA from the parked u, outputs, L2 lines dropped)"
+                    if path == "parked" else
                     "forward step: p3_prep_kernel + p3_agg_kernel (gate + chunk aggregates) + p3_carry_kernel + "
                     "p3_out_kernel" + (", two halves of the batch on two streams" if groups == 2 else ""))
 
@@ -414,8 +424,8 @@ def run_ours(args):
                          "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                          "peak_kind": peak_kind, "bytes_per_step": scan_bytes,
                          "avg_step_ms": scan_avg},
-            # the XU (MUFU) pipe: one reciprocal and one tanh per element in each of the two passes
-            "sfu": sfu_record(4 * elem, scan_avg, clocks, dev),
+            # the XU (MUFU) pipe: one reciprocal and one tanh per element in each evaluation pass
+            "sfu": sfu_record(2 * eval_passes * elem, scan_avg, clocks, dev),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": elem * 2 + B * D * 4,
                     "d2h_bytes_per_step": elem * 2 + B * D * 4},
             "clocks": clocks,

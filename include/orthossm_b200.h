@@ -121,13 +121,17 @@ int ossm_cheby_ema_fwd(const ossm_fwd_args* a, void* workspace, size_t workspace
 /* Which kernels ossm_cheby_ema_fwd runs for these arguments on the current
  * device (no launch): the generic kernel (any dtype / head size / mode), the
  * three-pass bf16 kernels (chunk aggregates, carry scan, outputs: 4 launches
- * per group of sequences), or the single-evaluation grouped kernel (one
- * cooperative launch, one CTA per SM, each sequence owned by a group of CTAs
- * that exchange tile aggregates through the workspace); -1 for invalid
- * arguments. */
+ * per group of sequences), the parked three-pass kernels (bf16 outputs
+ * contiguous along tokens, sequences of at most 24 MB of fp16 u: one setup
+ * launch, then per slab of sequences an aggregate pass that parks u in L2
+ * and forms the carries, and an output pass that reads u back), or the
+ * single-evaluation grouped kernel (one cooperative launch, one CTA per SM,
+ * each sequence owned by a group of CTAs that exchange tile aggregates
+ * through the workspace); -1 for invalid arguments. */
 #define OSSM_PATH_GENERIC 0
 #define OSSM_PATH_THREE_PASS 1
 #define OSSM_PATH_GROUPED 2
+#define OSSM_PATH_PARKED 3
 int ossm_fwd_path(const ossm_fwd_args* a);
 
 /* ossm_cheby_ema_fwd for callers that cannot allocate device memory (a host

@@ -20,7 +20,7 @@ OSSM_F_GENERIC = 1 << 4
 OSSM_F_SINGLE_EVAL = 1 << 5
 OSSM_F_ONE_STREAM = 1 << 7
 OSSM_NOALLOC_SCRATCH_BYTES = 16 << 20
-OSSM_PATH_GENERIC, OSSM_PATH_THREE_PASS, OSSM_PATH_GROUPED = 0, 1, 2
+OSSM_PATH_GENERIC, OSSM_PATH_THREE_PASS, OSSM_PATH_GROUPED, OSSM_PATH_PARKED = 0, 1, 2, 3
 
 EXPORTED = (
     "ossm_fwd_workspace_bytes", "ossm_fwd_path", "ossm_cheby_ema_fwd", "ossm_cheby_ema_fwd_noalloc", "ossm_gate_decay",

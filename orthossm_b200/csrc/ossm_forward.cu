@@ -420,6 +420,7 @@ using namespace ossm;
 
 bool ossm_p3_eligible(const ossm_fwd_args* a);
 size_t ossm_p3_workspace_bytes(const ossm_fwd_args* a);
+int ossm_p3_parked(const ossm_fwd_args* a);
 bool ossm_grp_eligible(const ossm_fwd_args* a);
 size_t ossm_grp_workspace_bytes(const ossm_fwd_args* a);
 int ossm_grp_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st);
@@ -550,7 +551,8 @@ extern "C" size_t ossm_fwd_workspace_bytes(const ossm_fwd_args* a) {
 extern "C" int ossm_fwd_path(const ossm_fwd_args* a) {
   if (validate_fwd(a) != OSSM_OK) return -1;
   if (!ossm_p3_eligible(a)) return OSSM_PATH_GENERIC;
-  return ossm_grp_eligible(a) ? OSSM_PATH_GROUPED : OSSM_PATH_THREE_PASS;
+  if (ossm_grp_eligible(a)) return OSSM_PATH_GROUPED;
+  return ossm_p3_parked(a) ? OSSM_PATH_PARKED : OSSM_PATH_THREE_PASS;
 }
 
 // Library-internal: where the generic kernel's look-back flags sit in the

@@ -1335,6 +1335,9 @@ int p3_launch_park(const ossm_fwd_args* a, int sb, char* ws, cudaStream_t st) {
 
 }  // namespace
 
+// Sequences per slab of the parked path for these (fast-path) arguments, or 0.
+int ossm_p3_parked(const ossm_fwd_args* a) { return p3_park_slab(a); }
+
 int ossm_p3_launch(const ossm_fwd_args* a, char* ws, cudaStream_t st) {
   if (const int sb = p3_park_slab(a)) return p3_launch_park(a, sb, ws, st);
   const int G = p3_groups(a);

@@ -226,13 +226,15 @@ def _fwd_args(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=
 
 def forward_path(x, coeffs, **kw):
     """Which kernels ``cheby_ema_forward(x, coeffs, **kw)`` runs on x's device:
-    "generic", "three_pass" or "grouped" (no launch)."""
+    "generic", "three_pass", "parked" (three-pass with u parked in L2) or
+    "grouped" (no launch)."""
     a, keep, _, _ = _fwd_args(x, coeffs, **kw)
     r = L.lib().ossm_fwd_path(L.C.byref(a))
     del keep
     if r < 0:
         L.check(L.OSSM_EINVAL, "forward_path (argument check)")
-    return {L.OSSM_PATH_GENERIC: "generic", L.OSSM_PATH_THREE_PASS: "three_pass", L.OSSM_PATH_GROUPED: "grouped"}[r]
+    return {L.OSSM_PATH_GENERIC: "generic", L.OSSM_PATH_THREE_PASS: "three_pass", L.OSSM_PATH_GROUPED: "grouped",
+            L.OSSM_PATH_PARKED: "parked"}[r]
 
 
 def cheby_ema_forward(x, coeffs, *, lambda_per_head=None, ema_momentum=0.9, gate_weight=None,

@@ -68,7 +68,7 @@ def test_grouped_vs_oracle(B, S, mode, init):
     kw, lt = _kw(mode, W, b, lam, B, S)
     from orthossm_b200 import _lib as L
     assert O.forward_path(T(x, torch.bfloat16), T(c), extra_flags=L.OSSM_F_SINGLE_EVAL, **kw) == "grouped"
-    assert O.forward_path(T(x, torch.bfloat16), T(c), **kw) == "three_pass"
+    assert O.forward_path(T(x, torch.bfloat16), T(c), **kw) == "parked"
     out, fin = _fwd(T(x, torch.bfloat16), T(c), init_state=T(ini) if init else None, **kw)
     torch.cuda.synchronize()
     assert O.workspace_status() == 0
