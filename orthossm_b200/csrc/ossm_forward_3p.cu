@@ -261,19 +261,24 @@ OSSM_DEV float lam_token(const Params& p, const float* lam_tok, int b, int tg, i
 // each chunk's carry and decay product from the span start (p.carry, p.P)
 // and the span's own record (spA, spE).  It then takes a ticket of the
 // sequence; the sequence's last folds the span records in span order into
-// the state entering each span (spX).  Each writer fences before its ticket
-// and each last CTA fences after it, so it reads every record the others
-// wrote; each resets its ticket for the next slab that uses this workspace.
+// the state entering each span (spX).  A CTA's threads write, meet at a
+// barrier, and one thread fences (cumulatively, for the whole CTA's writes)
+// and takes the ticket; a last CTA's ticket thread fences again before the
+// barrier after which its threads read the others' records.  Each last CTA
+// resets its ticket for the next slab that uses this workspace.
 // flag: one int of shared memory.
 OSSM_DEV void ring_carries(const Params& p, int b, int c, int h, int lane, int* flag) {
   const int tid = threadIdx.x, j0 = lane * 2;
   const int sp = c / kSpanC, c0 = sp * kSpanC, cnt = min(kSpanC, p.nchunks - c0);
-  __threadfence();
   __syncthreads();
-  if (tid == 0) *flag = atomicAdd(p.tk_span + (size_t)b * p.nsp + sp, 1u) == (uint32_t)(cnt - 1);
+  if (tid == 0) {
+    __threadfence();
+    const bool last = atomicAdd(p.tk_span + (size_t)b * p.nsp + sp, 1u) == (uint32_t)(cnt - 1);
+    if (last) __threadfence();
+    *flag = last;
+  }
   __syncthreads();
   if (!*flag) return;
-  __threadfence();
   const size_t nb = (size_t)(b * kH + h) * p.nchunks + c0;
   float2 X = make_float2(0.f, 0.f);
   float P = 1.f;
@@ -300,15 +305,16 @@ OSSM_DEV void ring_carries(const Params& p, int b, int c, int h, int lane, int* 
   const size_t ks = (size_t)(b * kH + h) * p.nsp;
   *reinterpret_cast<float2*>(p.spE + (ks + sp) * kHD + j0) = X;
   if (lane == 0) p.spA[ks + sp] = P;
-  __threadfence();
   __syncthreads();
   if (tid == 0) {
     p.tk_span[(size_t)b * p.nsp + sp] = 0u;
-    *flag = atomicAdd(p.tk_seq + b, 1u) == (uint32_t)(p.nsp - 1);
+    __threadfence();
+    const bool last = atomicAdd(p.tk_seq + b, 1u) == (uint32_t)(p.nsp - 1);
+    if (last) __threadfence();
+    *flag = last;
   }
   __syncthreads();
   if (!*flag) return;
-  __threadfence();
   X = make_float2(0.f, 0.f);
 #pragma unroll 1
   for (int s0 = 0; s0 < p.nsp; s0 += 8) {  // 8 span records per batch of loads
