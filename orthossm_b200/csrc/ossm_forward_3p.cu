@@ -24,9 +24,17 @@
 //                    rows instead and p3_outu_kernel reads it back (no second
 //                    evaluation).
 //
-// Every launch streams with high occupancy and no inter-CTA waits; the price is
-// a second evaluation and a second read of x.  Results are bitwise
-// reproducible (every fold has a fixed order).
+// bf16 outputs of sequences holding at most 24 MB of u take the parked path
+// instead: the batch runs as slabs of sequences on up to five streams, the
+// aggregate pass (ring mode) also parks each u as an fp16 pair in an
+// L2-resident ring slot and forms the carries itself (the last CTA of each
+// 16-chunk span, then of the sequence, folds the records: atomic tickets, no
+// waiting), and p3_outp_kernel reads u back from L2 and drops its lines, so
+// every element is evaluated once and x is read once.
+//
+// Every launch streams with high occupancy and no inter-CTA waits; on the
+// re-evaluating path the price is a second evaluation and a second read of
+// x.  Results are bitwise reproducible (every fold has a fixed order).
 //
 // NaN inputs are handled off the hot path: the fast evaluation lets them
 // surface as NaN, each warp checks its chunk once and recomputes it with the
