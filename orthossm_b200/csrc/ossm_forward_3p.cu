@@ -270,21 +270,24 @@ OSSM_DEV float lam_token(const Params& p, const float* lam_tok, int b, int tg, i
 // and the span's own record (spA, spE).  It then takes a ticket of the
 // sequence; the sequence's last folds the span records in span order into
 // the state entering each span (spX).  A CTA's threads write, meet at a
-// barrier, and one thread fences (cumulatively, for the whole CTA's writes)
-// and takes the ticket; a last CTA's ticket thread fences again before the
-// barrier after which its threads read the others' records.  Each last CTA
-// resets its ticket for the next slab that uses this workspace.
+// barrier, and one thread takes the ticket with an acquire-release atomic at
+// GPU scope (its release is cumulative over the CTA's writes ordered before
+// by the barrier; its acquire orders the records a last CTA's threads read
+// after the next barrier).  Each last CTA resets its ticket for the next
+// slab that uses this workspace.
 // flag: one int of shared memory.
+// Ticket with release (the CTA's writes, ordered before by the barrier) and
+// acquire (the records read after) semantics at GPU scope: the old count.
+OSSM_DEV uint32_t ticket_acq_rel(uint32_t* t) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(t) : "memory");
+  return old;
+}
 OSSM_DEV void ring_carries(const Params& p, int b, int c, int h, int lane, int* flag) {
   const int tid = threadIdx.x, j0 = lane * 2;
   const int sp = c / kSpanC, c0 = sp * kSpanC, cnt = min(kSpanC, p.nchunks - c0);
   __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const bool last = atomicAdd(p.tk_span + (size_t)b * p.nsp + sp, 1u) == (uint32_t)(cnt - 1);
-    if (last) __threadfence();
-    *flag = last;
-  }
+  if (tid == 0) *flag = ticket_acq_rel(p.tk_span + (size_t)b * p.nsp + sp) == (uint32_t)(cnt - 1);
   __syncthreads();
   if (!*flag) return;
   const size_t nb = (size_t)(b * kH + h) * p.nchunks + c0;
@@ -316,10 +319,7 @@ OSSM_DEV void ring_carries(const Params& p, int b, int c, int h, int lane, int* 
   __syncthreads();
   if (tid == 0) {
     p.tk_span[(size_t)b * p.nsp + sp] = 0u;
-    __threadfence();
-    const bool last = atomicAdd(p.tk_seq + b, 1u) == (uint32_t)(p.nsp - 1);
-    if (last) __threadfence();
-    *flag = last;
+    *flag = ticket_acq_rel(p.tk_seq + b) == (uint32_t)(p.nsp - 1);
   }
   __syncthreads();
   if (!*flag) return;
