@@ -40,8 +40,9 @@ def _chunked_relerr(a_bits, b_bits, rows=1 << 16):
 def test_config2_exact_bench_shape_vs_c_port():
     """BASELINE configs[1] as bench.py runs it: B=8 x S=16384 x D=512, bf16 in
     and out, fp32 state, the per-token gate, carried state N(0, 0.1), the
-    same seeded inputs; the default launch splits the batch over two
-    streams."""
+    same seeded inputs; the default launch takes the parked path (u kept in
+    L2 as fp16 between the two passes, eight one-sequence slabs on five
+    streams, carries formed by tickets in the aggregate pass)."""
     import bench
     import orthossm_b200 as O
     x_bits = bench.x_bits_host(1234)
@@ -53,6 +54,9 @@ def test_config2_exact_bench_shape_vs_c_port():
                                    init_state=torch.from_numpy(init).cuda())
     torch.cuda.synchronize()
     assert O.workspace_status() == 0
+    assert O.forward_path(x, torch.from_numpy(c).cuda(), lambda_per_head=torch.tensor(LAMBDA).cuda(),
+                          gate_weight=torch.from_numpy(W).cuda(), gate_bias=torch.from_numpy(b).cuda(),
+                          init_state=torch.from_numpy(init).cuda()) == "parked"
     ref_bits, ref_fin = cref.forward(x_bits, c, lam=lam, gate=dict(W=W, b=b), init=init, out_bf16=True,
                                      x_is_bf16_bits=True)
     got = _bits(out)
