@@ -1074,9 +1074,11 @@ int p3_params(const ossm_fwd_args* a, char* ws, p3::Params& p) {
 // would overwrite x another chunk still reads), and while the outputs fit in
 // half of L2, so the parked u is read back from L2.  Measured: the TTT step
 // of BASELINE.json configs[3] (16 forwards of 4 x 2048 tokens with fp32
-// states) went from 1.50 to 1.38 ms; for bf16 outputs, u parked as fp16 made
-// the config-2 step slower (122.8 -> 135.7 us): the extra 134 MB of writes
-// left L2 before the output pass read them.
+// states) went from 1.50 to 1.38 ms.  (bf16 outputs park u as fp16 in a
+// ring instead, slab by slab, so it stays in L2: the parked path below.
+// Parked in the rows of a whole batch of bf16 outputs, it made the config-2
+// step slower, 122.8 -> 135.7 us: its 134 MB left L2 before the output pass
+// read them.)
 int p3_uc_mode(const ossm_fwd_args* a) {
   if (a->out_dtype != OSSM_F32) return 0;
   const size_t D = (size_t)a->H * a->head_dim;
